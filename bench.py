@@ -1,0 +1,630 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 INT8 hot path on the BASELINE configs; prints ONE JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Default workload: block-scaled int8_gemm "expert up", M=4096 K=7168 N=2048,
+bf16 out, per GPU. With N GPUs (torchrun, one rank per GPU) the weight is sharded by N: global
+N = 2048 * world, each rank computes its own 2048 columns (weak scaling, no data-path collective).
+Other workloads: gemm_down (K=2048 N=7168, --m), act_quant (fp32/bf16 [2048, 7168]),
+index_prefill (4096 x 4096 causal, scores + top-2048), index_decode (4 x 32768 + top-2048),
+index_long (4096 queries x 131072 keys causal, keys sharded by range, all-gather merge).
+
+Timing: W untimed warm-up steps, then K steps between a barrier + synchronize on both sides,
+CUDA events on the launching stream, max over ranks. Inputs rotate over enough copies to exceed
+the 126 MB L2 between reuses. `value` = units of all ranks / max time. `e2e` repeats the step
+through the public API with pinned-host inputs copied in and the result copied out inside the
+timed region. `roofline` uses the dominant kernel's per-launch CUDA-event time.
+`--impl reference` times the CPU oracle port of reference.py (the reference's own CPU path) on a
+bounded sample of the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 2**20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ------------------------------------------------------------------------------------------ utils
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and clock-event reasons in a background thread."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x10: "sync_boost", 0x1: "gpu_idle"}
+
+    def __init__(self, device: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.ok = [], 0, False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            bus = None
+            try:
+                bus = torch.cuda.get_device_properties(device).pci_bus_id
+            except Exception:
+                pass
+            if bus:
+                try:
+                    self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus if isinstance(bus, bytes) else bus.encode())
+                except Exception:
+                    self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            else:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML unavailable: report it instead of guessing
+            self.err = str(e)
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                self.reasons |= int(self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._stop.clear()
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+            self._t = None
+
+    def summary(self, window: str):
+        if not self.ok:
+            return {"error": f"nvml unavailable: {getattr(self, 'err', '?')}"}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(names), "samples": len(self.samples), "window": window}
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------------------------------ workloads
+class Workload:
+    name = ""
+    metric = ""
+    unit = ""
+    higher_is_better = True
+    dtype = ""
+    scaling = "weak"
+    launches_per_step = 1
+
+    def value_from(self, units_per_step_all_ranks, ms_per_step):
+        raise NotImplementedError
+
+
+class GemmWorkload(Workload):
+    dtype = "int8"  # int8 x int8 -> int32 per 128-K block, fp32 promotion
+
+    def __init__(self, M, N, K, out, rank, world, label, seed=0):
+        self.M, self.N, self.K, self.out, self.rank, self.world = M, N, K, out, rank, world
+        self.name = label
+        self.metric = "block-scaled INT8 GEMM TOP/s"
+        self.unit = "TOP/s"
+        self.seed = seed
+        self.ops = 2.0 * M * N * K
+
+    def config(self):
+        return {"workload": f"int8_gemm {self.name} M={self.M} K={self.K} N={self.N} per GPU "
+                            f"(global N = {self.N}*world, sharded by N), out={self.out}",
+                "M": self.M, "K": self.K, "N_per_gpu": self.N, "out_dtype": self.out,
+                "parallelism": f"N-shard x{self.world}"}
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        from deepseek_v32_gtx1650_b200 import workloads as W
+        self.D = D
+        x, B, b_s = W.gemm_inputs(self.M, self.N * self.world, self.K, seed=self.seed)
+        lo, hi = self.rank * self.N, (self.rank + 1) * self.N
+        B, b_s = B[lo:hi].contiguous(), b_s[lo // 128:hi // 128].contiguous()
+        A, a_s = D.act_quant(x.to(dev))
+        self.host = (x, B, b_s)
+        self.odt = torch.bfloat16 if self.out == "bf16" else torch.float32
+        set_bytes = A.numel() + a_s.numel() * 4 + B.numel() + b_s.numel() * 4 + self.M * self.N * (2 if self.out == "bf16" else 4)
+        self.R = max(2, math.ceil(2 * L2_BYTES / set_bytes))
+        self.sets = []
+        for r in range(self.R):
+            self.sets.append((A.clone(), a_s.clone(), B.to(dev), b_s.to(dev),
+                              torch.empty(self.M, self.N, device=dev, dtype=self.odt)))
+        self.l2_note = f"{self.R} rotating input sets x {set_bytes / 1e6:.1f} MB (> 2 x 126 MB L2)"
+        self.bytes_alg = A.numel() + B.numel() + a_s.numel() * 4 + b_s.numel() * 4 + self.M * self.N * (2 if self.out == "bf16" else 4)
+
+    def step(self, i, ev=None):
+        A, a_s, B, b_s, C = self.sets[i % self.R]
+        if ev:
+            ev[0].record()
+        # public API, writes into a fresh tensor; C is kept only to hold the set's footprint
+        self.D.int8_gemm(A, a_s, B, b_s, out_dtype=self.odt)
+        if ev:
+            ev[1].record()
+
+    def units(self):
+        return self.ops
+
+    def value(self, ms, world):
+        return self.ops * world / (ms * 1e-3) / 1e12
+
+    # e2e: host pinned inputs -> device, public API call, result -> pinned host
+    def e2e_prepare(self, dev):
+        A, a_s, B, b_s, _ = self.sets[0]
+        self.hA, self.has_, self.hB, self.hbs = (t.cpu().pin_memory() for t in (A, a_s, B, b_s))
+        self.dA, self.das, self.dB, self.dbs = (torch.empty_like(t, device=dev) for t in (A, a_s, B, b_s))
+        self.hC = torch.empty(self.M, self.N, dtype=self.odt).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in (self.hA, self.has_, self.hB, self.hbs))
+        self.d2h = self.hC.numel() * self.hC.element_size()
+
+    def e2e_step(self):
+        self.dA.copy_(self.hA, non_blocking=True)
+        self.das.copy_(self.has_, non_blocking=True)
+        self.dB.copy_(self.hB, non_blocking=True)
+        self.dbs.copy_(self.hbs, non_blocking=True)
+        c = self.D.int8_gemm(self.dA, self.das, self.dB, self.dbs, out_dtype=self.odt)
+        self.hC.copy_(c, non_blocking=True)
+
+    def roofline(self, kernel_ms, peaks, src, traffic):
+        peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        ach = self.ops / (kernel_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
+                "frac": round(ach / peak, 4), "traffic": traffic.get(self.traffic_key()),
+                "peak_note": f"dense INT8 = 2 x {src} cuBLAS bf16 burst ({peaks.get('bf16_tflops')} TF/s); "
+                             f"nominal 4500 TOP/s",
+                "algorithmic_bytes": self.bytes_alg, "ops_per_launch": self.ops}
+
+    def traffic_key(self):
+        return f"int8_gemm_{self.name}"
+
+    def cpu_sample(self, seconds):
+        import oracle as O
+        x, B, b_s = self.host
+        rows = min(self.M, 128)
+        a, a_s = O.act_quant_ref(x[:rows].float().numpy())
+        Bn, bsn = B.numpy(), b_s.numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            O.int8_gemm_ref(a, a_s, Bn, bsn)
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = time.perf_counter() - t0
+        val = 2.0 * rows * self.N * self.K * n / dt / 1e12
+        return val, f"oracle int8_gemm_ref (float64 dequant + matmul, reference.py:18-24) on {rows} of {self.M} rows, {n} reps"
+
+
+class ActQuantWorkload(Workload):
+    def __init__(self, M, N, dt, rank, world):
+        self.M, self.N, self.dt = M, N, dt
+        self.name = f"act_quant_{dt}"
+        self.metric = "act_quant GB/s"
+        self.unit = "GB/s"
+        self.dtype = "fp32->int8" if dt == "fp32" else "bf16->int8"
+        self.tdt = torch.float32 if dt == "fp32" else torch.bfloat16
+        self.bytes = M * N * (torch.tensor([], dtype=self.tdt).element_size() + 1) + M * (N // 128) * 4
+
+    def config(self):
+        return {"workload": f"act_quant {self.dt} [{self.M}, {self.N}] -> int8 + fp32 scales"}
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        from deepseek_v32_gtx1650_b200 import workloads as W
+        self.D = D
+        x = W.act_quant_input(self.M, self.N).to(self.tdt)
+        self.host = x
+        self.R = max(2, math.ceil(2 * L2_BYTES / self.bytes))
+        self.sets = [x.to(dev) for _ in range(self.R)]
+        self.l2_note = f"{self.R} rotating inputs x {self.bytes / 1e6:.1f} MB"
+
+    def step(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        self.D.act_quant(self.sets[i % self.R])
+        if ev:
+            ev[1].record()
+
+    def value(self, ms, world):
+        return self.bytes * world / (ms * 1e-3) / 1e9
+
+    def e2e_prepare(self, dev):
+        self.hx = self.host.pin_memory()
+        self.dx = torch.empty_like(self.host, device=dev)
+        self.hy = torch.empty(self.M, self.N, dtype=torch.int8).pin_memory()
+        self.hs = torch.empty(self.M, self.N // 128, dtype=torch.float32).pin_memory()
+        self.h2d = self.hx.numel() * self.hx.element_size()
+        self.d2h = self.hy.numel() + self.hs.numel() * 4
+
+    def e2e_step(self):
+        self.dx.copy_(self.hx, non_blocking=True)
+        y, s = self.D.act_quant(self.dx)
+        self.hy.copy_(y, non_blocking=True)
+        self.hs.copy_(s, non_blocking=True)
+
+    def roofline(self, kernel_ms, peaks, src, traffic):
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        ach = self.bytes / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": traffic.get(self.name), "peak_note": f"{src} STREAM-style copy",
+                "algorithmic_bytes": self.bytes}
+
+    def cpu_sample(self, seconds):
+        import oracle as O
+        rows = min(self.M, 512)
+        x = self.host[:rows].float().numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            O.act_quant_ref(x)
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = time.perf_counter() - t0
+        b = rows * self.N * (self.tdt.itemsize + 1) + rows * (self.N // 128) * 4
+        return b * n / dt / 1e9, f"oracle act_quant_ref (reference.py:8-15) on {rows} of {self.M} rows, {n} reps"
+
+
+class IndexWorkload(Workload):
+    higher_is_better = False
+    dtype = "int8"
+    launches_per_step = 2
+
+    def __init__(self, kind, rank, world, topk=2048):
+        self.kind, self.rank, self.world, self.topk = kind, rank, world, topk
+        if kind == "prefill":
+            self.B, self.M, self.N, self.causal, self.start = 1, 4096, 4096, True, 0
+        elif kind == "decode":
+            self.B, self.M, self.N, self.causal, self.start = 1, 4, 32768, False, 0
+        else:  # long, keys sharded by range
+            self.B, self.M, self.N, self.causal, self.start = 1, 4096, 131072, True, 131072 - 4096
+        self.scaling = "strong" if kind == "long" else "weak"
+        self.name = f"index_{kind}"
+        self.metric = {"prefill": "indexer prefill ms @4096^2 causal (scores + top-2048)",
+                       "decode": "indexer decode ms (4 x 32768, scores + top-2048)",
+                       "long": "indexer long ms (4096 x 131072 causal, key-sharded, top-2048)"}[kind]
+        self.unit = "ms"
+        H, D = 64, 128
+        if self.causal:
+            pairs = sum(min(self.N, self.start + m + 1) for m in range(self.M))
+        else:
+            pairs = self.M * self.N
+        self.pairs = pairs * self.B
+        self.ops = 2.0 * self.pairs * H * D
+        self.ops_full = 2.0 * self.B * self.M * self.N * H * D
+
+    def config(self):
+        return {"workload": f"lightning indexer {self.kind}: B={self.B} M={self.M} N={self.N} H=64 D=128 "
+                            f"causal={self.causal} start={self.start}, top-{self.topk}",
+                "visible_pairs": self.pairs,
+                "parallelism": f"key-range x{self.world}" if self.kind == "long" else f"replicas x{self.world}"}
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        from deepseek_v32_gtx1650_b200 import workloads as W, sharded as S
+        self.D, self.S = D, S
+        q, w, k, ks = W.index_inputs(self.B, self.M, self.N, seed=0)
+        self.host = (q, w, k, ks)
+        if self.kind == "long":
+            self.lo, self.hi = S.shard_range(self.N, self.world, self.rank)
+            k, ks = k[:, self.lo:self.hi].contiguous(), ks[:, self.lo:self.hi].contiguous()
+        else:
+            self.lo, self.hi = 0, self.N
+        nloc = self.hi - self.lo
+        set_bytes = q.numel() + w.numel() * 4 + k.numel() + ks.numel() * 4 + self.B * self.M * nloc * 4
+        self.R = max(1, math.ceil(2 * L2_BYTES / set_bytes)) if set_bytes < 2 * L2_BYTES else 1
+        self.sets = [(q.to(dev), w.to(dev), k.to(dev), ks.to(dev)) for _ in range(self.R)]
+        self.scores = torch.empty(self.B, self.M, nloc, device=dev)
+        self.l2_note = f"{self.R} rotating input sets x {set_bytes / 1e6:.1f} MB"
+        self.bytes_alg = set_bytes
+
+    def step(self, i, ev=None):
+        q, w, k, ks = self.sets[i % self.R]
+        D = self.D
+        if self.kind == "long" and self.world > 1:
+            if ev:
+                ev[0].record()
+            self.S.sharded_index_topk(q, w, k, ks, self.lo, self.topk, self.causal, self.start)
+            if ev:
+                ev[1].record()
+            return
+        if ev:
+            ev[0].record()
+        sc = D.int8_index(q, w, k, ks, causal=self.causal, start=self.start - self.lo)
+        if ev:
+            ev[1].record()
+        D.select_topk(sc.view(self.B * self.M, -1), self.topk, idx_offset=self.lo)
+
+    def value(self, ms, world):
+        return ms
+
+    def e2e_prepare(self, dev):
+        q, w, k, ks = (t.pin_memory() for t in self.host)
+        if self.kind == "long":
+            k, ks = k[:, self.lo:self.hi].contiguous().pin_memory(), ks[:, self.lo:self.hi].contiguous().pin_memory()
+        self.hin = (q, w, k, ks)
+        self.din = tuple(torch.empty_like(t, device=dev) for t in self.hin)
+        self.hidx = torch.empty(self.B, self.M, self.topk, dtype=torch.int32).pin_memory()
+        self.hval = torch.empty(self.B, self.M, self.topk, dtype=torch.float32).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.hin)
+        self.d2h = self.hidx.numel() * 8
+
+    def e2e_step(self):
+        for d, h in zip(self.din, self.hin):
+            d.copy_(h, non_blocking=True)
+        q, w, k, ks = self.din
+        if self.kind == "long" and self.world > 1:
+            idx, vals = self.S.sharded_index_topk(q, w, k, ks, self.lo, self.topk, self.causal, self.start)
+        else:
+            idx, vals = self.D.int8_index_topk(q, w, k, ks, topk=self.topk, causal=self.causal,
+                                               start=self.start - self.lo, return_scores=False, key_offset=self.lo)
+        self.hidx.copy_(idx, non_blocking=True)
+        self.hval.copy_(vals, non_blocking=True)
+
+    def roofline(self, kernel_ms, peaks, src, traffic):
+        peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        ops = self.ops / (self.world if self.kind == "long" else 1)
+        ach = ops / (kernel_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
+                "frac": round(ach / peak, 4), "traffic": traffic.get(self.name),
+                "peak_note": f"dense INT8 = 2 x {src} cuBLAS bf16 burst; achieved counts visible (query, key) "
+                             f"pairs only", "ops_per_launch": ops,
+                "full_mn_convention_tops": round(self.ops_full / (self.world if self.kind == 'long' else 1)
+                                                 / (kernel_ms * 1e-3) / 1e12, 2)}
+
+    def cpu_sample(self, seconds):
+        import oracle as O
+        q, w, k, ks = (t.numpy() for t in self.host)
+        rows = np.arange(self.M) if self.M <= 16 else np.linspace(0, self.M - 1, 32).astype(np.int64)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            sc = O.int8_index_ref(q, w, k, ks, causal=self.causal, start=self.start, rows=rows)
+            O.topk_ref(sc, self.topk) if self.M <= 16 else None
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = (time.perf_counter() - t0) / n
+        if self.causal:
+            sample_pairs = sum(min(self.N, self.start + int(m) + 1) for m in rows)
+        else:
+            sample_pairs = len(rows) * self.N
+        ms_full = dt * 1e3 * (self.pairs / sample_pairs)
+        return ms_full, (f"oracle int8_index_ref (reference.py:27-34) on {len(rows)} of {self.M} query rows, "
+                         f"scaled by visible (query, key) pairs")
+
+
+def make_workload(args, rank, world):
+    if args.workload == "gemm_up":
+        return GemmWorkload(4096, 2048, 7168, "bf16", rank, world, "expert_up")
+    if args.workload == "gemm_down":
+        return GemmWorkload(args.m, 7168, 2048, args.out, rank, world, f"expert_down_m{args.m}", seed=1)
+    if args.workload == "act_quant":
+        return ActQuantWorkload(2048, 7168, args.aq_dtype, rank, world)
+    if args.workload in ("index_prefill", "index_decode", "index_long"):
+        return IndexWorkload(args.workload.split("_")[1], rank, world)
+    raise SystemExit(f"unknown workload {args.workload}")
+
+
+# ------------------------------------------------------------------------------------------ arms
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(os.cpu_count())
+    except Exception:
+        pass
+    wl = make_workload(args, 0, 1)
+    # inputs on the CPU only
+    import deepseek_v32_gtx1650_b200.workloads as W  # noqa: F401
+    if isinstance(wl, GemmWorkload):
+        x, B, b_s = W.gemm_inputs(wl.M, wl.N, wl.K, seed=wl.seed)
+        wl.host = (x, B, b_s)
+    elif isinstance(wl, ActQuantWorkload):
+        wl.host = W.act_quant_input(wl.M, wl.N).to(wl.tdt)
+    else:
+        wl.host = W.index_inputs(wl.B, wl.M, wl.N, seed=0)
+    per = args.ref_step_seconds
+    for _ in range(args.warmup):
+        wl.cpu_sample(0.0)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, sample = wl.cpu_sample(per)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    v = statistics.median(vals)
+    cores = cpu_threads()
+    line = {"impl": "reference", "metric": wl.metric, "value": round(v, 4), "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 2),
+            "higher_is_better": wl.higher_is_better, "scaling": wl.scaling, "vs_baseline": None,
+            "dtype": wl.dtype, "data": "synthetic (seeded)",
+            "config": wl.config(),
+            "cpu_baseline": {"value": round(v, 4), "unit": wl.unit, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(v, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import deepseek_v32_gtx1650_b200 as D
+    wl = make_workload(args, rank, world)
+    wl.prepare(dev)
+    peaks, src = load_peaks()
+    traffic = load_traffic()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        wl.step(i)
+    torch.cuda.synchronize()
+    code = D.device_status(local)
+    if code:
+        raise SystemExit(f"kernel reported an internal wait timeout during warm-up: {code:#x}")
+
+    sampler = ClockSampler(local)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    t_start.record()
+    for i in range(args.steps):
+        wl.step(i, evs[i])
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    sampler.stop()
+    ms = t_start.elapsed_time(t_end)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    window = "timed region"
+    if len(sampler.samples) < 5:  # timed region too short for NVML: sample a soak of the same step
+        window = "soak of the same step right after the timed region (timed region too short for NVML)"
+        sampler.start()
+        t0 = time.time()
+        i = 0
+        while time.time() - t0 < 0.6:
+            wl.step(i)
+            i += 1
+            if i % 32 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        sampler.stop()
+    t = torch.tensor([ms, kern_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kern_ms = float(t[0]), float(t[1])
+    ms_step = ms / args.steps
+    value = wl.value(ms_step, world)
+
+    # e2e through the public API with host buffers
+    wl.e2e_prepare(dev)
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        wl.e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_val = wl.value(float(e_ms), world)
+    code = D.device_status(local)
+
+    line = None
+    if rank == 0:
+        line = {"metric": wl.metric, "value": round(value, 4), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": wl.higher_is_better,
+                "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
+                "data": "synthetic (seeded generators with the BASELINE shapes and distributions)",
+                "config": dict(wl.config(), l2=wl.l2_note),
+                "e2e": {"value": round(e2e_val, 4), "unit": wl.unit, "h2d_bytes_per_step": int(wl.h2d),
+                        "d2h_bytes_per_step": int(wl.d2h), "steps": e2e_steps},
+                "roofline": wl.roofline(kern_ms, peaks, src, traffic),
+                "gpu_launches": args.steps * wl.launches_per_step,
+                "clocks": sampler.summary(window),
+                "device_error_word": code}
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                from threadpoolctl import threadpool_limits
+                threadpool_limits(os.cpu_count())
+            except Exception:
+                pass
+            v, sample = wl.cpu_sample(args.cpu_seconds)
+            line["cpu_baseline"] = {"value": round(v, 4), "unit": wl.unit, "cores": cpu_threads(), "kind": "port",
+                                    "sample": sample}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="gemm_up",
+                    choices=["gemm_up", "gemm_down", "act_quant", "index_prefill", "index_decode", "index_long"])
+    ap.add_argument("--m", type=int, default=32, help="M for gemm_down")
+    ap.add_argument("--out", default="bf16", choices=["bf16", "fp32"], help="output dtype for gemm_down")
+    ap.add_argument("--aq-dtype", default="fp32", choices=["fp32", "bf16"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=2.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

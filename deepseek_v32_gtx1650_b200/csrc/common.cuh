@@ -1,0 +1,223 @@
+// Shared sm_100a device helpers: mbarriers with bounded waits, TMA tile loads,
+// tcgen05 (TMEM alloc / MMA / ld / st / commit / fences) and UMMA descriptors.
+//
+// Everything here is written directly as inline PTX for sm_100a. Every spin on an
+// mbarrier is bounded: after DSV32_WAIT_LIMIT_CYCLES of SM clock the waiting thread
+// records an error word in device memory, raises the CTA's abort flag and returns
+// false, so the kernel winds down instead of hanging the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#define DSV32_DEV __device__ __forceinline__
+
+// ~1 s at 1.9 GHz. Normal waits in these kernels last microseconds.
+#ifndef DSV32_WAIT_LIMIT_CYCLES
+#define DSV32_WAIT_LIMIT_CYCLES 2000000000LL
+#endif
+
+// Error word shared by every kernel of the library (first error wins).
+// Layout: (kernel_id << 16) | site. Read and cleared by dsv32_device_status().
+__device__ unsigned int g_dsv32_device_error = 0;
+
+enum : unsigned int {
+  KID_GEMM = 1,
+  KID_INDEX = 2,
+};
+
+DSV32_DEV void record_device_error(unsigned int code) {
+  atomicCAS(&g_dsv32_device_error, 0u, code);
+}
+
+DSV32_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+DSV32_DEV uint32_t lane_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%laneid;" : "=r"(r));
+  return r;
+}
+
+// ---------------------------------------------------------------- mbarrier
+DSV32_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+DSV32_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+DSV32_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+DSV32_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+DSV32_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase of parity `parity` to complete. Returns false if the CTA
+// was aborted (by this or another thread) or the limit ran out.
+DSV32_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > DSV32_WAIT_LIMIT_CYCLES) {
+      *abort_flag = 1;
+      record_device_error(code);
+      return false;
+    }
+  }
+}
+
+// Same wait, made warp-uniform: every lane polls, and the warp proceeds only if all
+// lanes saw the phase complete. Required before .sync.aligned tcgen05 instructions.
+DSV32_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int code) {
+  bool ok = mbar_wait(bar, parity, abort_flag, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// ---------------------------------------------------------------- TMA
+DSV32_DEV void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+DSV32_DEV void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+DSV32_DEV void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+// TMEM allocation: executed by one whole warp; the base address lands in smem.
+DSV32_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+DSV32_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+DSV32_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+DSV32_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32, issued by a single thread.
+DSV32_DEV void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once) on an mbarrier when all previously issued tcgen05 MMAs of this thread complete.
+DSV32_DEV void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Instruction descriptor for kind::i8: signed A/B, s32 accumulator, both K-major.
+__host__ __device__ constexpr uint32_t make_idesc_i8(int m, int n) {
+  return (2u << 4)                          // D format: S32
+         | (1u << 7)                        // A format: signed int8
+         | (1u << 10)                       // B format: signed int8
+         | (uint32_t(n >> 3) << 17)         // N / 8
+         | (uint32_t(m >> 4) << 24);        // M / 16
+}
+
+// Shared-memory matrix descriptor for a K-major operand whose rows are `row_bytes`
+// long (64 or 128) and stored with the matching TMA swizzle; 8-row core groups are
+// 8 * row_bytes apart. The tile base must be aligned to 8 * row_bytes.
+DSV32_DEV uint64_t make_sdesc(uint32_t smem_addr, uint32_t row_bytes) {
+  const uint64_t swz = (row_bytes == 128) ? 2ull : 4ull;  // SWIZZLE_128B : SWIZZLE_64B
+  const uint64_t sbo = (8ull * row_bytes) >> 4;
+  return uint64_t((smem_addr >> 4) & 0x3FFFu)  // start address
+         | (1ull << 16)                        // leading byte offset (unused for swizzled K-major)
+         | (sbo << 32)                         // stride byte offset
+         | (1ull << 46)                        // descriptor version (sm_100)
+         | (swz << 61);                        // swizzle mode
+}
+
+// 32 lanes x 32 columns of 32-bit from TMEM into registers, then wait. The registers are
+// threaded through the wait so no use can be scheduled before the data has landed.
+DSV32_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// Fill 32 lanes x 32 columns of TMEM with one 32-bit value (no wait).
+DSV32_DEV void tmem_fill32(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+
+DSV32_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Register re-balancing between warpgroups (all 4 warps of a warpgroup execute it).
+template <uint32_t N>
+DSV32_DEV void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <uint32_t N>
+DSV32_DEV void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+
+// Named barrier over a subset of warps (ids 1..15; 0 is __syncthreads).
+DSV32_DEV void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// int32 accumulators are pre-biased with these bits: bits(1.5 * 2^23). For |x| < 2^22,
+// the bits (BIAS + x) read as a float equal 1.5 * 2^23 + x exactly, so one exact FADD of
+// -1.5 * 2^23 converts the tensor-core integer to fp32 (no I2F on the conversion pipe).
+constexpr uint32_t kI32FloatBiasBits = 0x4B400000u;
+constexpr float kI32FloatBias = 12582912.0f;

@@ -1,0 +1,347 @@
+// C-ABI entry points of libdsv32_int8.so (declared in include/dsv32_int8.h).
+//
+// One translation unit: it includes every kernel header so all kernels share the single
+// device error word g_dsv32_device_error. Host side: argument validation (the reference's
+// asserts), TMA tensor-map encoding through the driver entry point (no -lcuda needed),
+// per-device launch set-up, and the launches themselves.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include <cudaTypedefs.h>
+
+#include "../../include/dsv32_int8.h"
+#include "act_quant.cuh"
+#include "int8_gemm.cuh"
+#include "int8_index.cuh"
+#include "topk.cuh"
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int cuda_fail(cudaError_t e, const char* what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return DSV32_ERR_CUDA;
+}
+
+#define DSV32_CUDA_TRY(expr)                       \
+  do {                                             \
+    cudaError_t _e = (expr);                       \
+    if (_e != cudaSuccess) return cuda_fail(_e, #expr); \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceInfo {
+  bool ready = false;
+  bool sm100 = false;
+  int num_sms = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+template <typename K>
+cudaError_t set_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// Per-device set-up: SM count, architecture check, dynamic smem opt-in for every kernel.
+int device_setup(int* dev_out, DeviceInfo** info_out) {
+  int dev = 0;
+  DSV32_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return DSV32_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0;
+    DSV32_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    DSV32_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    DSV32_CUDA_TRY(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    d.sm100 = (major == 10 && minor == 0);
+    if (d.sm100) {
+      using namespace dsv32;
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<256, false>, gemm::Smem<256>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<256, true>, gemm::Smem<256>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<128, false>, gemm::Smem<128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128>, index::Cfg<64, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128>, index::Cfg<32, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128>, index::Cfg<16, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 64>, index::Cfg<64, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 64>, index::Cfg<32, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64>, index::Cfg<16, 64>::kAlloc));
+      if (!g_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        DSV32_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) {
+          t_last_error = "cuTensorMapEncodeTiled entry point not found";
+          return DSV32_ERR_CUDA;
+        }
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      }
+    }
+    d.ready = true;
+  }
+  if (!d.sm100) return DSV32_ERR_NO_DEVICE;
+  *dev_out = dev;
+  *info_out = &d;
+  return DSV32_OK;
+}
+
+// Tiled int8 tensor map over a row-major array: dims listed innermost first, strides in bytes
+// for dims 1.., box sizes per dim. Swizzle chosen from the inner box width (64 or 128 bytes).
+int encode_i8_map(CUtensorMap* map, const void* ptr, int rank, const uint64_t* dims, const uint64_t* strides,
+                  const uint32_t* box) {
+  uint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle swz = (box[0] == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_error = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
+    return DSV32_ERR_CUDA;
+  }
+  return DSV32_OK;
+}
+
+int launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return DSV32_OK;
+}
+
+int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype, int64_t m,
+              int64_t n, int64_t k, int32_t* partials, void* stream) {
+  if (!a || !a_s || !b || !b_s || !c) return DSV32_ERR_INVALID_ARG;
+  if (m < 1 || n < 1 || k < 1) return DSV32_ERR_INVALID_ARG;
+  if (k % 128 != 0 || n % 128 != 0) return DSV32_ERR_UNSUPPORTED;
+  if (c_dtype != DSV32_F32 && c_dtype != DSV32_BF16 && c_dtype != DSV32_F16) return DSV32_ERR_INVALID_ARG;
+  if (m > (1LL << 31) - 1 || n > (1LL << 31) - 1 || k > (1LL << 31) - 1) return DSV32_ERR_UNSUPPORTED;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return DSV32_ERR_INVALID_ARG;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+
+  // Narrow tiles when there are too few 128x256 tiles to cover the SMs, or N is an odd
+  // multiple of 128.
+  const int64_t tiles256 = ((m + 127) / 128) * ((n + 255) / 256);
+  const bool bn128 = !partials && ((n % 256) != 0 || tiles256 < info->num_sms);
+  const int BN = bn128 ? 128 : 256;
+
+  CUtensorMap tmA, tmB;
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(k)};
+  const uint32_t boxA[2] = {128, 128};
+  const uint32_t boxB[2] = {128, static_cast<uint32_t>(BN)};
+  if (int st = encode_i8_map(&tmA, a, 2, dimsA, strides, boxA)) return st;
+  if (int st = encode_i8_map(&tmB, b, 2, dimsB, strides, boxB)) return st;
+
+  const int64_t tiles = ((m + 127) / 128) * ((n + BN - 1) / BN);
+  const int grid = static_cast<int>(tiles < info->num_sms ? tiles : info->num_sms);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace dsv32::gemm;
+  if (partials) {
+    int8_gemm_kernel<256, true><<<grid, kThreads, Smem<256>::kAlloc, st>>>(
+        tmA, tmB, a_s, b_s, c, kOutF32, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), partials);
+  } else if (BN == 256) {
+    int8_gemm_kernel<256, false><<<grid, kThreads, Smem<256>::kAlloc, st>>>(
+        tmA, tmB, a_s, b_s, c, static_cast<uint32_t>(c_dtype), static_cast<int>(m), static_cast<int>(n),
+        static_cast<int>(k), nullptr);
+  } else {
+    int8_gemm_kernel<128, false><<<grid, kThreads, Smem<128>::kAlloc, st>>>(
+        tmA, tmB, a_s, b_s, c, static_cast<uint32_t>(c_dtype), static_cast<int>(m), static_cast<int>(n),
+        static_cast<int>(k), nullptr);
+  }
+  return launch_check("int8_gemm_kernel launch");
+}
+
+template <int H, int D>
+int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w, const float* k_s, float* out,
+                 int64_t batch, int64_t m, int64_t n, int causal, int64_t start, int num_sms, cudaStream_t st) {
+  using namespace dsv32::index;
+  using C = Cfg<H, D>;
+  const int64_t nqb = (m + C::QB - 1) / C::QB;
+  const int64_t nt = (n + kKeysPerTile - 1) / kKeysPerTile;
+  // Chunk the key tiles so that there are at least ~2 waves of work units.
+  const int64_t want_units = 2LL * num_sms;
+  int64_t chunks = (want_units + batch * nqb - 1) / (batch * nqb);
+  if (chunks < 1) chunks = 1;
+  if (chunks > nt) chunks = nt;
+  int64_t tpc = (nt + chunks - 1) / chunks;
+  chunks = (nt + tpc - 1) / tpc;
+  const int64_t units = batch * nqb * chunks;
+  if (units > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
+  int8_index_kernel<H, D><<<static_cast<unsigned>(units), kThreads, C::kAlloc, st>>>(
+      tmQ, tmK, w, k_s, out, static_cast<int>(m), static_cast<int>(n), causal, static_cast<long long>(start),
+      static_cast<int>(tpc), static_cast<int>(chunks));
+  return launch_check("int8_index_kernel launch");
+}
+
+int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
+               int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, void* stream) {
+  if (!q || !w || !k || !k_s || !out) return DSV32_ERR_INVALID_ARG;
+  if (batch < 1 || m < 1 || n < 1) return DSV32_ERR_INVALID_ARG;
+  if (!((heads == 16 || heads == 32 || heads == 64) && (dim == 64 || dim == 128))) return DSV32_ERR_UNSUPPORTED;
+  if (m * heads > (1LL << 31) - 1 || n > (1LL << 31) - 1 || batch > 65535) return DSV32_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k)) return DSV32_ERR_INVALID_ARG;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+  const int qb = static_cast<int>(256 / heads);
+  CUtensorMap tmQ, tmK;
+  const uint64_t dimsQ[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(m * heads),
+                             static_cast<uint64_t>(batch)};
+  const uint64_t strQ[2] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(m * heads * dim)};
+  const uint32_t boxQ[3] = {static_cast<uint32_t>(dim), static_cast<uint32_t>(qb * heads), 1};
+  const uint64_t dimsK[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(n), static_cast<uint64_t>(batch)};
+  const uint64_t strK[2] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(n * dim)};
+  const uint32_t boxK[3] = {static_cast<uint32_t>(dim), 128, 1};
+  if (int st = encode_i8_map(&tmQ, q, 3, dimsQ, strQ, boxQ)) return st;
+  if (int st = encode_i8_map(&tmK, k, 3, dimsK, strK, boxK)) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int S = info->num_sms;
+#define DSV32_INDEX_CASE(HH, DD) \
+  if (heads == HH && dim == DD) return index_launch<HH, DD>(tmQ, tmK, w, k_s, out, batch, m, n, causal, start, S, st);
+  DSV32_INDEX_CASE(64, 128)
+  DSV32_INDEX_CASE(32, 128)
+  DSV32_INDEX_CASE(16, 128)
+  DSV32_INDEX_CASE(64, 64)
+  DSV32_INDEX_CASE(32, 64)
+  DSV32_INDEX_CASE(16, 64)
+#undef DSV32_INDEX_CASE
+  return DSV32_ERR_UNSUPPORTED;
+}
+
+int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
+              int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
+  if (!scores || !out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
+  if (rows < 1 || n < 1 || k < 1 || k > n || ld < n) return DSV32_ERR_INVALID_ARG;
+  if (cand_idx && cand_ld < n) return DSV32_ERR_INVALID_ARG;
+  if (n > (1LL << 31) - 1 || rows > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace dsv32::topk;
+  const unsigned g = static_cast<unsigned>(rows);
+  const int nn = static_cast<int>(n), kk = static_cast<int>(k);
+  if (n <= 256 * 4) {
+    topk_reg_kernel<256, 4><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+  } else if (n <= 256 * 16) {
+    topk_reg_kernel<256, 16><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+  } else if (n <= 512 * 16) {
+    topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+  } else {
+    topk_radix_kernel<1024><<<g, 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+  }
+  return launch_check("topk kernel launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int dsv32_abi_version(void) { return DSV32_ABI_VERSION; }
+
+const char* dsv32_status_string(int status) {
+  switch (status) {
+    case DSV32_OK: return "ok";
+    case DSV32_ERR_INVALID_ARG: return "invalid argument";
+    case DSV32_ERR_UNSUPPORTED: return "unsupported shape";
+    case DSV32_ERR_CUDA: return "CUDA error";
+    case DSV32_ERR_DEVICE_TIMEOUT: return "kernel timed out on an internal wait";
+    case DSV32_ERR_NO_DEVICE: return "current device is not an sm_100 GPU";
+    default: return "unknown status";
+  }
+}
+
+const char* dsv32_last_error_message(void) { return t_last_error.c_str(); }
+
+int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int round_scale, int8_t* y, float* s,
+                    void* stream) {
+  if (!x || !y || !s) return DSV32_ERR_INVALID_ARG;
+  if (rows < 0 || n < 0) return DSV32_ERR_INVALID_ARG;
+  if (n % 128 != 0) return DSV32_ERR_UNSUPPORTED;
+  if (x_dtype != DSV32_F32 && x_dtype != DSV32_BF16 && x_dtype != DSV32_F16) return DSV32_ERR_INVALID_ARG;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(y) & 7u) != 0 || (reinterpret_cast<uintptr_t>(s) & 3u) != 0)
+    return DSV32_ERR_INVALID_ARG;
+  const int64_t groups = rows * (n / 128);
+  if (groups == 0) return DSV32_OK;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  constexpr int kUnroll = 4;
+  const int threads = 256;
+  const int gpw = (x_dtype == DSV32_F32) ? 1 : 2;
+  const int64_t slots = (groups + gpw - 1) / gpw;
+  const int64_t warps_needed = (slots + kUnroll - 1) / kUnroll;
+  int64_t blocks = (warps_needed + (threads / 32) - 1) / (threads / 32);
+  const int64_t cap = static_cast<int64_t>(info->num_sms) * 8;  // 8 resident CTAs per SM
+  if (blocks > cap) blocks = cap;
+  using namespace dsv32;
+  if (x_dtype == DSV32_F32) {
+    act_quant_kernel<float, kUnroll><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+        static_cast<const float*>(x), y, s, groups, round_scale);
+  } else if (x_dtype == DSV32_BF16) {
+    act_quant_kernel<__nv_bfloat16, kUnroll><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), y, s, groups, round_scale);
+  } else {
+    act_quant_kernel<__half, kUnroll><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+        static_cast<const __half*>(x), y, s, groups, round_scale);
+  }
+  return launch_check("act_quant_kernel launch");
+}
+
+int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,
+                    int64_t m, int64_t n, int64_t k, void* stream) {
+  return gemm_impl(a, a_s, b, b_s, c, c_dtype, m, n, k, nullptr, stream);
+}
+
+int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, float* c,
+                             int32_t* partials, int64_t m, int64_t n, int64_t k, void* stream) {
+  if (!partials) return DSV32_ERR_INVALID_ARG;
+  return gemm_impl(a, a_s, b, b_s, c, DSV32_F32, m, n, k, partials, stream);
+}
+
+int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
+                     int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, void* stream) {
+  return index_impl(q, w, k, k_s, out, batch, m, n, heads, dim, causal, start, stream);
+}
+
+int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
+               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
+  return topk_impl(scores, rows, n, ld, cand_idx, cand_ld, idx_offset, k, out_idx, out_val, stream);
+}
+
+int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,
+                          int64_t batch, int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start,
+                          int64_t topk, int32_t* out_idx, float* out_val, void* stream) {
+  if (topk < 1 || topk > n) return DSV32_ERR_INVALID_ARG;
+  if (!out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
+  if (int st = index_impl(q, w, k, k_s, scores, batch, m, n, heads, dim, causal, start, stream)) return st;
+  return topk_impl(scores, batch * m, n, n, nullptr, 0, 0, topk, out_idx, out_val, stream);
+}
+
+int dsv32_device_status(int device, uint32_t* code) {
+  if (!code) return DSV32_ERR_INVALID_ARG;
+  int prev = 0;
+  DSV32_CUDA_TRY(cudaGetDevice(&prev));
+  if (prev != device) DSV32_CUDA_TRY(cudaSetDevice(device));
+  cudaError_t e = cudaDeviceSynchronize();
+  unsigned int v = 0;
+  const unsigned int zero = 0;
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_dsv32_device_error, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_dsv32_device_error, &zero, sizeof(zero));
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "dsv32_device_status");
+  *code = v;
+  return v ? DSV32_ERR_DEVICE_TIMEOUT : DSV32_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,317 @@
+// int8_index: DeepSeek-V3.2 lightning indexer on the sm_100a tensor cores.
+//
+//   score[b, m, n] = k_s[b, n] * sum_h w[b, m, h] * relu( sum_d q[b, m, h, d] * k[b, n, d] )
+//   causal: score = -inf where n > start + m
+//
+// Semantics: reference.py:27-34 (int8_index_ref) and kernels.py:134-162. Operands keep the
+// reference layout: q [B, M, H, D] int8, k [B, N, D] int8, w [B, M, H] fp32, k_s [B, N] fp32,
+// out [B, M, N] fp32.
+//
+// Mapping (one CTA per work unit = (batch, block of QB queries, chunk of 128-key tiles)):
+//   UMMA M = 128 keys (TMEM lanes), UMMA N = QB*H (query, head) pairs (QB*H = 256), K = D.
+//   Each epilogue thread owns one key and reduces relu(logit) * w over the heads of its
+//   queries entirely in registers (no cross-lane reduction), then scales by k_s and stores.
+//   warp 8 = TMA producer (Q block once, then a 4-stage ring of key tiles),
+//   warp 9 = MMA issuer (double-buffered int32 TMEM accumulator), warps 0-7 = epilogue;
+//   warp w reads TMEM lanes 32*(w%4).. and the query half w/4 of the columns.
+// Key tiles past the causal limit of every query in the block are not loaded or multiplied:
+// the epilogue writes -inf for them directly (the reference's tile skip, kernels.py:145-148).
+//
+// relu and the int32 -> fp32 conversion use the same pre-biased accumulator as int8_gemm:
+// bits = bits(1.5*2^23) + logit, so relu is an integer max against the bias bits and the
+// conversion is one exact FADD. |logit| <= D*127*127 < 2^21.
+#pragma once
+#include "common.cuh"
+
+namespace dsv32 {
+namespace index {
+
+constexpr int kKeysPerTile = 128;
+constexpr int kStages = 4;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 idle
+// Launch: 384 threads x 168 registers = 64512. setmaxnreg moves them to the epilogue:
+// 2 warpgroups x 128 x 200 + 1 warpgroup x 128 x 104 = 64512 (and per sub-partition
+// 200 + 200 + 104 = 504 <= 512).
+constexpr uint32_t kEpiRegs = 200;
+constexpr uint32_t kCtlRegs = 104;
+constexpr int kProducerWarp = kEpiWarps;
+constexpr int kMmaWarp = kEpiWarps + 1;
+constexpr int kNmma = 256;  // QB * H
+
+template <int H, int D>
+struct Cfg {
+  static constexpr int QB = kNmma / H;                 // queries per block
+  static constexpr int kQBytes = QB * H * D;           // Q tile bytes
+  static constexpr int kKBytes = kKeysPerTile * D;     // key tile bytes per stage
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffW = kOffK + kStages * kKBytes;
+  static constexpr int kOffBar = kOffW + QB * H * 4;
+  // qfull, kfull[kStages], kempty[kStages], tfull[2], tempty[2], mma_done
+  static constexpr int kNumBars = 2 + 2 * kStages + 4;
+  static constexpr int kOffTmem = kOffBar + 8 * kNumBars;
+  static constexpr int kOffAbort = kOffTmem + 4;
+  static constexpr int kBytes = kOffAbort + 4;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(QB * H == kNmma, "QB*H must be 256");
+  static_assert(D == 64 || D == 128, "head dim must be 64 or 128");
+  static_assert(QB % 2 == 0, "two query halves");
+  static constexpr int kColsPerHalf = kNmma / 2;       // columns per epilogue warpgroup
+  static constexpr int kQPerHalf = QB / 2;
+};
+
+DSV32_DEV void drain_wait(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > DSV32_WAIT_LIMIT_CYCLES / 16) break;
+  }
+}
+
+struct Unit {
+  int b, m0, kt0, kt_vis, kt1;
+};
+
+// Work unit of this CTA. Units are ordered so the heaviest causal query blocks start first.
+DSV32_DEV Unit decode_unit(int M, int N, int QB, int causal, long long start, int tiles_per_chunk,
+                           int num_chunks) {
+  const int NQB = (M + QB - 1) / QB;
+  const int NT = (N + kKeysPerTile - 1) / kKeysPerTile;
+  const int idx = blockIdx.x;
+  const int c = idx % num_chunks;
+  const int rest = idx / num_chunks;
+  int qb = rest % NQB;
+  if (causal) qb = NQB - 1 - qb;
+  Unit u;
+  u.b = rest / NQB;
+  u.m0 = qb * QB;
+  u.kt0 = c * tiles_per_chunk;
+  u.kt1 = min(NT, u.kt0 + tiles_per_chunk);
+  u.kt_vis = u.kt1;
+  if (causal) {
+    const long long m_last = min(M - 1, u.m0 + QB - 1);
+    const long long lim = start + m_last + 1;  // keys [0, lim) are visible to some query
+    const long long vis_tiles = (lim + kKeysPerTile - 1) / kKeysPerTile;
+    u.kt_vis = static_cast<int>(max(static_cast<long long>(u.kt0), min(static_cast<long long>(u.kt1), vis_tiles)));
+  }
+  return u;
+}
+
+template <int H, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    int8_index_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const float* __restrict__ w, const float* __restrict__ k_s, float* __restrict__ out, int M,
+                      int N, int causal, long long start, int tiles_per_chunk, int num_chunks) {
+  using C = Cfg<H, D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_base);
+
+  const uint32_t sQ = base + C::kOffQ;
+  const uint32_t sK = base + C::kOffK;
+  float* sW = reinterpret_cast<float*>(smem + C::kOffW);
+  const uint32_t bar0 = base + C::kOffBar;
+  const uint32_t qfull_bar = bar0;
+  auto kfull_bar = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto kempty_bar = [&](int s) { return bar0 + 8u * (1 + kStages + s); };
+  auto tfull_bar = [&](int b) { return bar0 + 8u * (1 + 2 * kStages + b); };
+  auto tempty_bar = [&](int b) { return bar0 + 8u * (3 + 2 * kStages + b); };
+  const uint32_t mma_done_bar = bar0 + 8u * (5 + 2 * kStages);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffAbort);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const Unit un = decode_unit(M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
+  const int n_mma_tiles = un.kt_vis - un.kt0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull_bar, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(kfull_bar(s), 1);
+      mbar_init(kempty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), kEpiWarps);
+    }
+    mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) tmem_alloc(smem_u32(tmem_slot), 2 * kNmma);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp >= kEpiWarps) {
+    regs_dec<kCtlRegs>();
+  }
+  if (warp == kProducerWarp) {
+    if (lane == 0 && n_mma_tiles > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      mbar_arrive_expect_tx(qfull_bar, C::kQBytes);
+      tma_load_3d(sQ, &tmQ, qfull_bar, 0, un.m0 * H, un.b);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int kt = un.kt0; kt < un.kt_vis; ++kt) {
+        if (!mbar_wait(kempty_bar(stage), phase ^ 1u, abort_flag, (KID_INDEX << 16) | 1)) break;
+        mbar_arrive_expect_tx(kfull_bar(stage), C::kKBytes);
+        tma_load_3d(sK + stage * C::kKBytes, &tmK, kfull_bar(stage), 0, kt * kKeysPerTile, un.b);
+        ++issued;
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      for (int i = 0; i < kStages && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = kStages - 1;
+          phase ^= 1u;
+        }
+        drain_wait(kfull_bar(stage), phase);
+      }
+      drain_wait(qfull_bar, 0);
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && n_mma_tiles > 0) {
+      constexpr uint32_t idesc = make_idesc_i8(kKeysPerTile, kNmma);
+      bool ok = mbar_wait(qfull_bar, 0, abort_flag, (KID_INDEX << 16) | 2);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; ok && i < n_mma_tiles; ++i) {
+        const uint32_t buf = uint32_t(i) & 1u;
+        if (!mbar_wait(tempty_bar(buf), (uint32_t(i) >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 3) ||
+            !mbar_wait(kfull_bar(stage), phase, abort_flag, (KID_INDEX << 16) | 4))
+          break;
+        tc_fence_after();
+        const uint32_t k_addr = sK + stage * C::kKBytes;
+        const uint32_t d_tmem = tmem_base + buf * kNmma;
+#pragma unroll
+        for (int k = 0; k < D / 32; ++k) {
+          umma_i8(d_tmem, make_sdesc(k_addr + 32 * k, D), make_sdesc(sQ + 32 * k, D), idesc, 1u);
+        }
+        umma_commit(kempty_bar(stage));
+        umma_commit(tfull_bar(buf));
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      umma_commit(mma_done_bar);
+      drain_wait(mma_done_bar, 0);
+    }
+  } else if (warp < kEpiWarps) {
+    regs_inc<kEpiRegs>();
+    // ------------------------------------------------------------ epilogue (256 threads)
+    const int wq = warp & 3;
+    const int wh = warp >> 2;
+    const int et = threadIdx.x;  // 0..255
+    // Head weights of the query block -> smem (rows past M read as 0).
+    for (int i = et; i < C::QB * H; i += kEpiWarps * 32) {
+      const int m = un.m0 + i / H;
+      sW[i] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (i % H)) : 0.f;
+    }
+    named_bar_sync(1, kEpiWarps * 32);
+
+    const int q_first = wh * C::kQPerHalf;  // first query (within the block) of this half
+    const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wh * C::kColsPerHalf);
+    float* out_b = out + static_cast<int64_t>(un.b) * M * N;
+    bool ok = true;
+
+    if (n_mma_tiles > 0) {
+      const float4* w_half = reinterpret_cast<const float4*>(sW + wh * C::kColsPerHalf);
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+#pragma unroll
+        for (int c = 0; c < C::kColsPerHalf / 32; ++c) tmem_fill32(t_lane + b * kNmma + c * 32, kI32FloatBiasBits);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(tempty_bar(0));
+        mbar_arrive(tempty_bar(1));
+      }
+      const float2 nbias = make_float2(-kI32FloatBias, -kI32FloatBias);
+      for (int i = 0; i < n_mma_tiles; ++i) {
+        const uint32_t buf = uint32_t(i) & 1u;
+        const int n = (un.kt0 + i) * kKeysPerTile + wq * 32 + lane;
+        const float ks = (n < N) ? __ldg(k_s + static_cast<int64_t>(un.b) * N + n) : 0.f;
+        if (!mbar_wait_warp(tfull_bar(buf), (uint32_t(i) >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float2 acc[C::kQPerHalf];
+#pragma unroll
+        for (int q = 0; q < C::kQPerHalf; ++q) acc[q] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < C::kColsPerHalf / 32; ++c) {
+          uint32_t r[32];
+          const uint32_t ta = t_lane + buf * kNmma + c * 32;
+          tmem_ld32(ta, r);
+          tmem_fill32(ta, kI32FloatBiasBits);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 w4 = w_half[c * 8 + j4];  // same address across the warp: broadcast
+            const int q = (c * 32 + 4 * j4) / H;   // query of these 4 columns (compile time)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int j = 4 * j4 + 2 * h;
+              const int r0 = max(static_cast<int>(r[j]), static_cast<int>(kI32FloatBiasBits));
+              const int r1 = max(static_cast<int>(r[j + 1]), static_cast<int>(kI32FloatBiasBits));
+              float2 v = make_float2(__int_as_float(r0), __int_as_float(r1));
+              v = __fadd2_rn(v, nbias);  // exact relu(logit) in fp32
+              const float2 wv = h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
+              acc[q] = __ffma2_rn(v, wv, acc[q]);
+            }
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(buf));
+        if (n < N) {
+#pragma unroll
+          for (int q = 0; q < C::kQPerHalf; ++q) {
+            const int m = un.m0 + q_first + q;
+            if (m < M) {
+              float sc = (acc[q].x + acc[q].y) * ks;
+              if (causal && static_cast<long long>(n) > start + m) sc = -INFINITY;
+              out_b[static_cast<int64_t>(m) * N + n] = sc;
+            }
+          }
+        }
+      }
+    }
+    // Tiles that no query of this block can see: -inf without loading or multiplying.
+    if (ok) {
+      for (int kt = un.kt_vis; kt < un.kt1; ++kt) {
+        const int n = kt * kKeysPerTile + wq * 32 + lane;
+        if (n < N) {
+#pragma unroll
+          for (int q = 0; q < C::kQPerHalf; ++q) {
+            const int m = un.m0 + q_first + q;
+            if (m < M) out_b[static_cast<int64_t>(m) * N + n] = -INFINITY;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, 2 * kNmma);
+  }
+}
+
+}  // namespace index
+}  // namespace dsv32

@@ -1,0 +1,162 @@
+"""Drop-in replacements for the reference's kernels.py API, backed by libdsv32_int8.so (sm_100a).
+
+Same names, argument meaning, return shapes and assert behaviour as the reference
+(kernels.py:55 act_quant, :109 int8_gemm, :165 int8_index). Tuning keywords of the Triton
+versions (block_m, version, block_q, block_n, num_warps) are accepted and ignored: tile
+shapes are fixed per shape class inside the CUDA library.
+
+Every op runs the CUDA library on the input's device and current stream; there is no CPU
+path. Calling with CPU tensors raises, as the reference's Triton launch would.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+GROUP = 128  # quantisation block (kernels.py:19)
+
+_DT = {torch.float32: _lib.DSV32_F32, torch.bfloat16: _lib.DSV32_BF16, torch.float16: _lib.DSV32_F16}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("deepseek_v32_gtx1650_b200 kernels run on CUDA tensors only (no CPU path)")
+
+
+def act_quant(x: torch.Tensor, round_scale: bool = False, block_m: int = 32):
+    """x [..., N] -> (int8 [..., N], fp32 scales [..., N // 128]). kernels.py:55-64."""
+    assert x.is_contiguous() and x.shape[-1] % GROUP == 0
+    assert x.dtype in _DT, f"act_quant supports float32/bfloat16/float16, got {x.dtype}"
+    _require_cuda(x)
+    N = x.shape[-1]
+    x2 = x.view(-1, N)
+    M = x2.shape[0]
+    NG = N // GROUP
+    y = torch.empty_like(x2, dtype=torch.int8)
+    s = torch.empty(M, NG, device=x.device, dtype=torch.float32)
+    if M > 0 and N > 0:
+        with torch.cuda.device(x.device):
+            _lib.check(_lib.load().dsv32_act_quant(x2.data_ptr(), _DT[x.dtype], M, N, int(bool(round_scale)),
+                                                   y.data_ptr(), s.data_ptr(), _stream(x)), "act_quant")
+    return y.view(x.shape), s.view(*x.shape[:-1], NG)
+
+
+def int8_gemm(a, a_s, b, b_s, out_dtype=torch.float32, version="v1"):
+    """a [..., K] int8, a_s [..., K // 128], b [N, K] int8, b_s [N // 128, K // 128] -> [..., N].
+    kernels.py:109-127."""
+    assert a.is_contiguous() and b.is_contiguous() and a_s.is_contiguous() and b_s.is_contiguous()
+    K = a.shape[-1]
+    N = b.shape[0]
+    M = a.numel() // K if K else 0
+    KG = K // GROUP
+    assert K % GROUP == 0 and N % GROUP == 0
+    assert a.dtype == torch.int8 and b.dtype == torch.int8 and b.shape[1] == K
+    assert a_s.dtype == torch.float32 and b_s.dtype == torch.float32
+    assert a_s.numel() == M * KG and b_s.numel() == (N // GROUP) * KG
+    assert out_dtype in _DT, f"unsupported out_dtype {out_dtype}"
+    _require_cuda(a, a_s, b, b_s)
+    c = torch.empty(*a.shape[:-1], N, device=a.device, dtype=out_dtype)
+    if M > 0 and N > 0 and K > 0:
+        with torch.cuda.device(a.device):
+            _lib.check(_lib.load().dsv32_int8_gemm(a.data_ptr(), a_s.data_ptr(), b.data_ptr(), b_s.data_ptr(),
+                                                   c.data_ptr(), _DT[out_dtype], M, N, K, _stream(a)), "int8_gemm")
+    return c
+
+
+def int8_gemm_partials(a, a_s, b, b_s):
+    """Debug form of int8_gemm on the same tensor-core path: returns (c fp32 [M, N],
+    partials int32 [K // 128, M, N]) where partials[kb] is the exact integer A_kb . B_kb^T."""
+    assert a.is_contiguous() and b.is_contiguous() and a_s.is_contiguous() and b_s.is_contiguous()
+    K = a.shape[-1]
+    N = b.shape[0]
+    M = a.numel() // K
+    assert K % GROUP == 0 and N % GROUP == 0 and a.dtype == torch.int8 and b.dtype == torch.int8
+    _require_cuda(a, a_s, b, b_s)
+    c = torch.empty(M, N, device=a.device, dtype=torch.float32)
+    p = torch.empty(K // GROUP, M, N, device=a.device, dtype=torch.int32)
+    with torch.cuda.device(a.device):
+        _lib.check(_lib.load().dsv32_int8_gemm_partials(a.data_ptr(), a_s.data_ptr(), b.data_ptr(), b_s.data_ptr(),
+                                                        c.data_ptr(), p.data_ptr(), M, N, K, _stream(a)),
+                   "int8_gemm_partials")
+    return c, p
+
+
+def _index_checks(q, w, k, k_s):
+    assert q.dim() == 4 and k.dim() == 3, "q [b, m, h, d], k [b, n, d]"
+    B, M, H, D = q.shape
+    assert q.is_contiguous() and k.is_contiguous() and w.is_contiguous() and k_s.is_contiguous()
+    assert k.shape[0] == B and k.shape[2] == D
+    assert q.dtype == torch.int8 and k.dtype == torch.int8
+    assert w.dtype == torch.float32 and k_s.dtype == torch.float32
+    assert w.shape == (B, M, H) and k_s.shape == (B, k.shape[1])
+    return B, M, H, D, k.shape[1]
+
+
+def int8_index(q, w, k, k_s, causal=False, start=0, block_q=None, block_n=None, num_warps=None):
+    """q [b, m, h, d] int8, w [b, m, h] fp32, k [b, n, d] int8, k_s [b, n] fp32 -> [b, m, n] fp32.
+    causal: keys after start + m get -inf. kernels.py:165-178."""
+    B, M, H, D, Nk = _index_checks(q, w, k, k_s)
+    _require_cuda(q, w, k, k_s)
+    o = torch.empty(B, M, Nk, device=q.device, dtype=torch.float32)
+    if B and M and Nk:
+        with torch.cuda.device(q.device):
+            _lib.check(_lib.load().dsv32_int8_index(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
+                                                    o.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start),
+                                                    _stream(q)), "int8_index")
+    return o
+
+
+def select_topk(scores: torch.Tensor, k: int, idx_offset: int = 0, cand_idx: torch.Tensor | None = None):
+    """Top-k of every row of scores [..., n] fp32 -> (idx int32 [..., k], vals fp32 [..., k]).
+
+    Replaces torch.topk on indexer scores. The k largest values are kept, ties at the k-th value
+    go to the lowest positions, and results are listed in increasing position order (not by
+    value). idx = position + idx_offset, or cand_idx[..., position] when cand_idx is given
+    (merging candidate lists from key-range shards)."""
+    assert scores.dtype == torch.float32 and scores.is_contiguous()
+    n = scores.shape[-1]
+    assert 1 <= k <= n, "k must be in [1, n]"
+    _require_cuda(scores)
+    rows = scores.numel() // n if n else 0
+    idx = torch.empty(*scores.shape[:-1], k, device=scores.device, dtype=torch.int32)
+    vals = torch.empty(*scores.shape[:-1], k, device=scores.device, dtype=torch.float32)
+    if cand_idx is not None:
+        assert cand_idx.dtype == torch.int32 and cand_idx.is_contiguous() and cand_idx.shape == scores.shape
+        cp, cld = cand_idx.data_ptr(), n
+    else:
+        cp, cld = None, 0
+    if rows:
+        with torch.cuda.device(scores.device):
+            _lib.check(_lib.load().dsv32_topk(scores.data_ptr(), rows, n, n, cp, cld, int(idx_offset), k,
+                                              idx.data_ptr(), vals.data_ptr(), _stream(scores)), "select_topk")
+    return idx, vals
+
+
+def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_scores=True, key_offset=0):
+    """Indexer scores + per-query top-k in one call (the step bench_indexer_e2e.py:54-57,72-77 runs).
+
+    Returns (scores [b, m, n], idx int32 [b, m, topk], vals fp32 [b, m, topk]), or (idx, vals) when
+    return_scores is False. idx are key positions (+ key_offset), in increasing order per query;
+    see select_topk for the tie rule."""
+    B, M, H, D, Nk = _index_checks(q, w, k, k_s)
+    assert 1 <= topk <= Nk, "topk must be in [1, n]"
+    _require_cuda(q, w, k, k_s)
+    scores = torch.empty(B, M, Nk, device=q.device, dtype=torch.float32)
+    idx = torch.empty(B, M, topk, device=q.device, dtype=torch.int32)
+    vals = torch.empty(B, M, topk, device=q.device, dtype=torch.float32)
+    if B and M:
+        lib = _lib.load()
+        with torch.cuda.device(q.device):
+            s = _stream(q)
+            _lib.check(lib.dsv32_int8_index(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
+                                            scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start), s),
+                       "int8_index_topk")
+            _lib.check(lib.dsv32_topk(scores.data_ptr(), B * M, Nk, Nk, None, 0, int(key_offset), topk,
+                                      idx.data_ptr(), vals.data_ptr(), s), "int8_index_topk")
+    return (scores, idx, vals) if return_scores else (idx, vals)

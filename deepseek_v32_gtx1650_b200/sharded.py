@@ -1,0 +1,81 @@
+"""Multi-GPU partitioning of the hot path, one process per GPU over torch.distributed (NCCL).
+
+Only the two paths that shard naturally are partitioned:
+
+- int8_gemm by N: rank r owns a contiguous range of whole 128-column weight blocks (its rows of
+  B and b_s); A and a_s are replicated. The kernel needs no collective. gather_columns()
+  optionally all-gathers the column slices into the full [M, N] output.
+- The indexer by key range: rank r owns keys [lo, hi) of the key cache (lo a multiple of 128).
+  It scores every query against its keys with the causal limit shifted by -lo, selects its local
+  top-k (global key ids = lo + position), and the (value, id) lists are all-gathered over
+  NVLink. Every rank then merges the world * k candidates with the same top-k kernel. Local lists
+  are position-ordered and concatenated in rank order, so ties resolve to the lowest global key
+  id exactly as in the single-GPU selection; the merged result is identical to it.
+
+The reference has no multi-GPU code (single GTX 1650); these are the two exchange patterns its
+hot path admits.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import kernels as K
+
+
+def shard_range(n: int, world: int, rank: int, align: int = 128) -> tuple[int, int]:
+    """Contiguous [lo, hi) of n items for `rank`, boundaries on multiples of `align` (the last
+    shard takes the remainder). Shards are as equal as the alignment allows."""
+    units = (n + align - 1) // align
+    base, extra = divmod(units, world)
+    lo_u = rank * base + min(rank, extra)
+    hi_u = lo_u + base + (1 if rank < extra else 0)
+    return min(n, lo_u * align), min(n, hi_u * align)
+
+
+def local_causal_start(start: int, lo: int) -> int:
+    """Causal limit for a key shard starting at global key `lo`: query m sees global keys
+    n <= start + m, i.e. local keys j <= (start - lo) + m."""
+    return start - lo
+
+
+def gather_candidates(idx: torch.Tensor, vals: torch.Tensor, group=None):
+    """All-gather per-rank top-k lists ([rows, k] int32 ids, [rows, k] fp32 values) and return
+    the candidates of every row concatenated in rank order: ([rows, world*k] int32, fp32).
+    One collective: ids and value bits travel together as int32."""
+    world = dist.get_world_size(group)
+    rows, k = idx.shape
+    packed = torch.stack([idx, vals.view(torch.int32)]).contiguous()  # [2, rows, k]
+    out = torch.empty((world,) + tuple(packed.shape), dtype=torch.int32, device=packed.device)
+    dist.all_gather_into_tensor(out, packed, group=group)
+    cand = out.permute(1, 2, 0, 3).reshape(2, rows, world * k)  # row-major: rank 0's k, rank 1's k, ...
+    return cand[0].contiguous(), cand[1].contiguous().view(torch.float32)
+
+
+def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, causal: bool = False,
+                       start: int = 0, group=None):
+    """Key-range sharded indexer + top-k. q [B, M, H, D], w [B, M, H] replicated; k_local [B, n_r, D],
+    k_s_local [B, n_r] this rank's keys starting at global key key_lo. Returns (idx int32 [B, M, topk],
+    vals fp32 [B, M, topk]) on every rank, identical to the single-GPU int8_index_topk."""
+    B, M = q.shape[:2]
+    assert k_local.shape[1] >= topk, "each key shard must hold at least topk keys"
+    idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
+                                  start=local_causal_start(start, key_lo), return_scores=False,
+                                  key_offset=key_lo)
+    cidx, cval = gather_candidates(idx.view(B * M, topk), vals.view(B * M, topk), group)
+    midx, mval = K.select_topk(cval, topk, cand_idx=cidx)
+    return midx.view(B, M, topk), mval.view(B, M, topk)
+
+
+def sharded_int8_gemm(a, a_s, b_local, b_s_local, out_dtype=torch.float32):
+    """N-sharded block-scaled GEMM: this rank's output columns [M, n_r] from its weight rows."""
+    return K.int8_gemm(a, a_s, b_local, b_s_local, out_dtype=out_dtype)
+
+
+def gather_columns(c_local: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather equal-width column slices [M, n_r] into the full [M, world * n_r] output."""
+    world = dist.get_world_size(group)
+    M, nr = c_local.shape
+    out = torch.empty(world, M, nr, dtype=c_local.dtype, device=c_local.device)
+    dist.all_gather_into_tensor(out, c_local.contiguous(), group=group)
+    return out.permute(1, 0, 2).reshape(M, world * nr)

@@ -1,0 +1,110 @@
+/* dsv32_int8.h - C ABI of the B200 (sm_100a) INT8 hot-path kernels.
+ *
+ * This is the drop-in boundary for the three INT8 kernels of hamzak-27/deepseek-v32-gtx1650
+ * (act_quant, int8_gemm, int8_index) plus the fused top-k selection the indexer feeds.
+ * Every entry point takes plain device pointers, element counts and a CUDA stream
+ * (passed as `void*`, a cudaStream_t; NULL = legacy default stream), launches
+ * asynchronously on that stream and returns a status code. No torch types appear here.
+ *
+ * Conventions shared by all entry points
+ *  - All pointers are device pointers to contiguous row-major arrays, 16-byte aligned.
+ *  - Outputs are caller-allocated; inputs are never written. Nothing here allocates device
+ *    memory except the per-device launch set-up on first use (function attributes).
+ *  - Status codes: DSV32_OK on success; DSV32_ERR_* otherwise (see dsv32_status_string()).
+ *    Argument errors are detected before any launch. Kernels that time out on an internal
+ *    wait report it through dsv32_device_status().
+ *  - Entry points may be called from any host thread; they keep no mutable global state
+ *    apart from a per-device, mutex-guarded set-up cache.
+ */
+#ifndef DSV32_INT8_H_
+#define DSV32_INT8_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSV32_ABI_VERSION 1
+
+/* Status codes. */
+#define DSV32_OK 0
+#define DSV32_ERR_INVALID_ARG 1     /* null pointer, bad size, misaligned pointer */
+#define DSV32_ERR_UNSUPPORTED 2     /* shape the reference asserts on (K % 128, N % 128, ...) */
+#define DSV32_ERR_CUDA 3            /* a CUDA runtime/driver call failed */
+#define DSV32_ERR_DEVICE_TIMEOUT 4  /* a kernel gave up on an internal wait (dsv32_device_status) */
+#define DSV32_ERR_NO_DEVICE 5       /* current device is not an sm_100 GPU */
+
+/* Element types. */
+#define DSV32_F32 0
+#define DSV32_BF16 1
+#define DSV32_F16 2
+
+/* act_quant: replaces kernels.py:55 act_quant(x, round_scale, block_m) and its kernel
+ * kernels.py:37-52 (oracle reference.py:8-15).
+ * x [rows, n] (x_dtype: DSV32_F32 / DSV32_BF16 / DSV32_F16), n % 128 == 0.
+ * y [rows, n] int8; s [rows, n / 128] fp32. Per 128-wide group: s = max(amax, 1e-4) * (1/127),
+ * or its ue8m0 power of two when round_scale != 0; y = clamp(round_half_even(x / s), +-127). */
+int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int round_scale, int8_t* y, float* s,
+                    void* stream);
+
+/* int8_gemm: replaces kernels.py:109 int8_gemm(a, a_s, b, b_s, out_dtype, version) and its kernel
+ * kernels.py:71-101 (oracle reference.py:18-24).
+ * a [m, k] int8, a_s [m, k/128] fp32, b [n, k] int8, b_s [n/128, k/128] fp32,
+ * c [m, n] of c_dtype (DSV32_F32 / DSV32_BF16 / DSV32_F16). k % 128 == 0, n % 128 == 0, any m >= 1.
+ * c[i, j] = sum_kb fp32(A_kb . B_kb) * (a_s[i, kb] * b_s[j / 128, kb]), accumulated in fp32. */
+int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,
+                    int64_t m, int64_t n, int64_t k, void* stream);
+
+/* Debug form of dsv32_int8_gemm (same tensor-core path): also writes the exact int32 partial of
+ * every 128-wide K block, partials [k/128, m, n] int32, and c [m, n] fp32. For parity tests. */
+int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, float* c,
+                             int32_t* partials, int64_t m, int64_t n, int64_t k, void* stream);
+
+/* int8_index: replaces kernels.py:165 int8_index(q, w, k, k_s, causal, start, ...) and its kernel
+ * kernels.py:134-162 (oracle reference.py:27-34).
+ * q [batch, m, heads, dim] int8, w [batch, m, heads] fp32, k [batch, n, dim] int8, k_s [batch, n] fp32,
+ * out [batch, m, n] fp32. (heads, dim) in {16, 32, 64} x {64, 128}.
+ * out[b, i, j] = k_s[b, j] * sum_h w[b, i, h] * relu(q[b, i, h, :] . k[b, j, :]);
+ * causal != 0: out = -inf where j > start + i (start may be negative: a key shard whose first
+ * key lies past some queries' positions). */
+int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
+                     int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, void* stream);
+
+/* Top-k selection per row: replaces torch.topk(scores, k) on the indexer output
+ * (test_kernels.py:125, bench_indexer_e2e.py:72-77).
+ * Row r of the input is scores[r * ld + 0 .. n). Selects the k largest values (ties at the k-th
+ * value: lowest position first) and writes them in increasing position order:
+ * out_idx [rows, k] int32, out_val [rows, k] fp32. The index written for position p is
+ * cand_idx[r * cand_ld + p] when cand_idx is non-NULL (merging candidate lists), else p + idx_offset
+ * (a shard's first global key). Requires 1 <= k <= n. */
+int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
+               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream);
+
+/* Indexer + top-k in one call (bench_indexer_e2e.py:54-57,72-77): scores are written to the
+ * caller's `scores` buffer [batch, m, n] fp32 (workspace; it also holds the full scores on return),
+ * then the top `topk` keys of every (batch, query) row are selected as dsv32_topk does.
+ * out_idx / out_val [batch, m, topk]. Requires 1 <= topk <= n. */
+int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,
+                          int64_t batch, int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start,
+                          int64_t topk, int32_t* out_idx, float* out_val, void* stream);
+
+/* Synchronises `device`, then reads and clears its kernel error word. *code = 0 if no kernel
+ * gave up on an internal wait since the last call; else (kernel_id << 16) | site. Returns
+ * DSV32_ERR_DEVICE_TIMEOUT when *code != 0. */
+int dsv32_device_status(int device, uint32_t* code);
+
+/* Human-readable text for a status code (static storage). */
+const char* dsv32_status_string(int status);
+
+/* Text of the last CUDA error seen by an entry point on this host thread (static per thread). */
+const char* dsv32_last_error_message(void);
+
+/* DSV32_ABI_VERSION of the loaded library. */
+int dsv32_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV32_INT8_H_ */

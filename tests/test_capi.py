@@ -1,0 +1,74 @@
+"""The C-ABI library builds, loads and exports every entry point include/dsv32_int8.h declares; argument
+validation (which runs before any CUDA call) returns the documented status codes. CPU only."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+from deepseek_v32_gtx1650_b200 import _lib, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "dsv32_int8.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(dsv32_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_lists_entry_points():
+    names = declared_functions()
+    assert "dsv32_act_quant" in names and "dsv32_int8_gemm" in names and "dsv32_int8_index" in names
+    assert set(names) == set(_lib.SIGNATURES), "ctypes table and header disagree"
+
+
+def test_library_builds_and_exports_every_symbol():
+    path = build.build()
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (dsv32_\w+)$", out, flags=re.M))
+    missing = set(declared_functions()) - exported
+    assert not missing, f"not exported: {missing}"
+    lib = _lib.load()
+    for name in declared_functions():
+        assert getattr(lib, name) is not None
+
+
+def test_abi_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.dsv32_abi_version() == 1
+    for code in range(6):
+        assert lib.dsv32_status_string(code)
+    assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")
+
+
+def test_argument_validation_without_gpu():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)  # never dereferenced: validation rejects before any launch
+    # null pointers
+    assert lib.dsv32_act_quant(None, 0, 4, 128, 0, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_gemm(None, fake, fake, fake, fake, 0, 1, 128, 128, None) == _lib.DSV32_ERR_INVALID_ARG
+    # the reference's shape asserts: N % 128, K % 128
+    assert lib.dsv32_act_quant(fake, 0, 4, 100, 0, fake, fake, None) == _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 128, 100, None) == _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 100, 128, None) == _lib.DSV32_ERR_UNSUPPORTED
+    # bad dtype code, bad head configuration, bad top-k
+    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 7, 4, 128, 128, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_index(fake, fake, fake, fake, fake, 1, 4, 128, 48, 128, 0, 0, None) == \
+        _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_topk(fake, 4, 100, 100, None, 0, 0, 101, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_index_topk(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 0, fake, fake,
+                                     None) == _lib.DSV32_ERR_INVALID_ARG
+    # misaligned operand
+    odd = ctypes.c_void_p(4096 + 4)
+    assert lib.dsv32_int8_gemm(odd, fake, fake, fake, fake, 0, 4, 128, 128, None) == _lib.DSV32_ERR_INVALID_ARG
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_no_device_is_an_error_not_a_fallback():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    st = lib.dsv32_act_quant(fake, 0, 4, 128, 0, fake, fake, None)
+    assert st in (_lib.DSV32_ERR_CUDA, _lib.DSV32_ERR_NO_DEVICE)

@@ -1,0 +1,84 @@
+"""act_quant on the B200 against the reference: bit-exact values and scales (test_kernels.py:21-45,
+BASELINE config 0 at full size)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import deepseek_v32_gtx1650_b200 as D
+from deepseek_v32_gtx1650_b200 import workloads
+from tests.golden.make_golden import adversarial_groups
+from tests.gpu_util import DEV, assert_no_device_error, bf16_from_bits, cuda, f32_of, npy
+
+pytestmark = pytest.mark.gpu
+DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+@pytest.mark.parametrize("dn", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("rs", [0, 1])
+def test_act_quant_matches_reference_golden(golden, dn, rs):
+    for si in range(int(golden["aq_nshapes"])):
+        xg = golden[f"aq_{si}_{dn}_x"]
+        x = bf16_from_bits(xg) if dn == "bf16" else cuda(xg)
+        y, s = D.act_quant(x, bool(rs))
+        assert y.dtype == torch.int8 and y.shape == x.shape and s.shape == (*x.shape[:-1], x.shape[-1] // 128)
+        np.testing.assert_array_equal(npy(s), golden[f"aq_{si}_{dn}_r{rs}_s"])
+        np.testing.assert_array_equal(npy(y), golden[f"aq_{si}_{dn}_r{rs}_y"])
+    assert_no_device_error()
+
+
+def test_act_quant_zero_and_tiny(golden):
+    y, s = D.act_quant(cuda(golden["aq_zero_x"]))
+    np.testing.assert_array_equal(npy(y), golden["aq_zero_y"])
+    np.testing.assert_array_equal(npy(s), golden["aq_zero_s"])
+
+
+@pytest.mark.parametrize("rs", [0, 1])
+def test_act_quant_adversarial_ue8m0(golden, rs):
+    x = cuda(adversarial_groups(golden["aq_adv_amax"]))
+    y, s = D.act_quant(x, bool(rs))
+    np.testing.assert_array_equal(npy(s), golden[f"aq_adv_r{rs}_s"])
+    np.testing.assert_array_equal(npy(y), golden[f"aq_adv_r{rs}_y"])
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rs", [False, True])
+def test_act_quant_baseline_config_full_size(dt, rs):
+    """[2048, 7168] with outliers and a zero row, both scale formats, bit-exact."""
+    x = workloads.act_quant_input(2048, 7168, seed=0).to(dt)
+    y, s = D.act_quant(x.to(DEV), rs)
+    yr, sr = O.act_quant_ref(f32_of(x), rs)
+    np.testing.assert_array_equal(npy(s), sr)
+    np.testing.assert_array_equal(npy(y), yr)
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("shape", [(3, 5, 7, 256), (1, 128), (777, 384), (64, 7168)])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16])
+def test_act_quant_odd_shapes(shape, dt):
+    g = torch.Generator().manual_seed(sum(shape))
+    x = (torch.randn(shape, generator=g) * 3).to(dt)
+    x.view(-1)[::97] *= 50
+    for rs in (False, True):
+        y, s = D.act_quant(x.to(DEV), rs)
+        yr, sr = O.act_quant_ref(f32_of(x), rs)
+        np.testing.assert_array_equal(npy(s), sr)
+        np.testing.assert_array_equal(npy(y), yr)
+
+
+def test_act_quant_roundtrip_error():
+    x = torch.randn(64, 1024, generator=torch.Generator().manual_seed(1)).to(DEV)
+    y, s = D.act_quant(x)
+    deq = y.float().view(64, 8, 128) * s.unsqueeze(-1)
+    assert (deq.view_as(x) - x).abs().max() <= s.max() / 2 + 1e-6  # error at most half a step
+
+
+def test_act_quant_empty_and_nan():
+    y, s = D.act_quant(torch.zeros(0, 256, device=DEV))
+    assert y.shape == (0, 256) and s.shape == (0, 2)
+    x = torch.randn(2, 256)
+    x[1, 3] = float("nan")
+    y, s = D.act_quant(x.to(DEV))
+    _, sr = O.act_quant_ref(x.numpy())
+    assert np.isnan(npy(s)[1, 0]) and np.isnan(sr[1, 0])  # NaN propagates to the group scale like torch.amax
+    np.testing.assert_array_equal(npy(s)[0], sr[0])

@@ -136,6 +136,7 @@ class Workload:
     dtype = ""
     scaling = "weak"
     launches_per_step = 1
+    graphable = True  # the timed steps can be captured in one CUDA graph
 
     def value_from(self, units_per_step_all_ranks, ms_per_step):
         raise NotImplementedError
@@ -323,6 +324,7 @@ class IndexWorkload(Workload):
         else:  # long, keys sharded by range
             self.B, self.M, self.N, self.causal, self.start = 1, 4096, 131072, True, 131072 - 4096
         self.scaling = "strong" if kind == "long" else "weak"
+        self.graphable = not (kind == "long" and world > 1)  # NCCL all-gather stays eager
         self.name = f"index_{kind}"
         self.metric = {"prefill": "indexer prefill ms @4096^2 causal (scores + top-2048)",
                        "decode": "indexer decode ms (4 x 32768, scores + top-2048)",
@@ -362,9 +364,12 @@ class IndexWorkload(Workload):
         self.l2_note = f"{self.R} rotating input sets x {set_bytes / 1e6:.1f} MB"
         self.bytes_alg = set_bytes
 
-    def step(self, i, ev=None):
+    def step(self, i, ev=None, main_only=False):
         q, w, k, ks = self.sets[i % self.R]
         D = self.D
+        if main_only:
+            D.int8_index(q, w, k, ks, causal=self.causal, start=self.start - self.lo)
+            return
         if self.kind == "long" and self.world > 1:
             if ev:
                 ev[0].record()
@@ -522,32 +527,68 @@ def run_ours(args):
         raise SystemExit(f"kernel reported an internal wait timeout during warm-up: {code:#x}")
 
     sampler = ClockSampler(local)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def capture(fn):
+        """One CUDA graph of the given launches (warm-up above has allocated every workspace)."""
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()  # allocations of this replay-shaped sequence happen outside the capture
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=side):  # same stream as the warm-up: workspaces reused
+            fn()
+        torch.cuda.synchronize()
+        return g
+
+    graph = kgraph = None
+    if wl.graphable:
+        graph = capture(lambda: [wl.step(i) for i in range(args.steps)])
+        if wl.launches_per_step > 1:
+            kgraph = capture(lambda: [wl.step(i, main_only=True) for i in range(args.steps)])
+    evs = None if graph is not None else [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                                          for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     sampler.start()
     t_start.record()
-    for i in range(args.steps):
-        wl.step(i, evs[i])
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(args.steps):
+            wl.step(i, evs[i])
     t_end.record()
     torch.cuda.synchronize()
     barrier()
     sampler.stop()
     ms = t_start.elapsed_time(t_end)
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    if graph is not None:
+        if kgraph is not None:  # the dominant kernel alone, back to back
+            k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            k0.record()
+            kgraph.replay()
+            k1.record()
+            torch.cuda.synchronize()
+            kern_ms = k0.elapsed_time(k1) / args.steps
+        else:
+            kern_ms = ms / args.steps
+    else:
+        kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     window = "timed region"
-    if len(sampler.samples) < 5:  # timed region too short for NVML: sample a soak of the same step
+    if len(sampler.samples) < 5 and not args.profile:  # timed region too short for NVML: sample a soak of the same step
         window = "soak of the same step right after the timed region (timed region too short for NVML)"
         sampler.start()
         t0 = time.time()
         i = 0
         while time.time() - t0 < 0.6:
-            wl.step(i)
-            i += 1
-            if i % 32 == 0:
-                torch.cuda.synchronize()
-        torch.cuda.synchronize()
+            if graph is not None:
+                graph.replay()
+            else:
+                wl.step(i)
+                i += 1
+            torch.cuda.synchronize()
         sampler.stop()
     t = torch.tensor([ms, kern_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -558,8 +599,8 @@ def run_ours(args):
 
     # e2e through the public API with host buffers
     wl.e2e_prepare(dev)
-    e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(2):
+    e2e_steps = 0 if args.profile else max(3, min(args.steps, 20))
+    for _ in range(2 if e2e_steps else 0):
         wl.e2e_step()
     torch.cuda.synchronize()
     barrier()
@@ -569,7 +610,7 @@ def run_ours(args):
         wl.e2e_step()
     e1.record()
     torch.cuda.synchronize()
-    e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
+    e_ms = torch.tensor([e0.elapsed_time(e1) / max(e2e_steps, 1)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     e2e_val = wl.value(float(e_ms), world)
@@ -586,6 +627,8 @@ def run_ours(args):
                         "d2h_bytes_per_step": int(wl.d2h), "steps": e2e_steps},
                 "roofline": wl.roofline(kern_ms, peaks, src, traffic),
                 "gpu_launches": args.steps * wl.launches_per_step,
+                "timing": "CUDA graph of the K steps, replayed once between events" if graph is not None
+                          else "eager launches, CUDA events per launch",
                 "clocks": sampler.summary(window),
                 "device_error_word": code}
         if world == 1 and not args.no_cpu_baseline:
@@ -618,7 +661,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="for ncu captures: timed steps only (no clock soak, e2e or CPU baseline)")
     args = ap.parse_args()
+    if args.profile:
+        args.no_cpu_baseline = True
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         run_reference_arm(args)

@@ -29,8 +29,9 @@ _i32 = ctypes.c_int
 # name -> (restype, argtypes); mirrors include/dsv32_int8.h
 SIGNATURES = {
     "dsv32_act_quant": (_i32, [_p, _i32, _i64, _i64, _i32, _p, _p, _p]),
-    "dsv32_int8_gemm": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _p]),
-    "dsv32_int8_gemm_partials": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "dsv32_int8_gemm": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _p, _i64, _p]),
+    "dsv32_int8_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "dsv32_int8_gemm_partials": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "dsv32_int8_index": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _p]),
     "dsv32_topk": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p]),
     "dsv32_int8_index_topk": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _p, _p,
@@ -82,9 +83,14 @@ def check(status: int, where: str) -> None:
 
 
 def device_status(device: int = 0) -> int:
-    """Synchronise `device` and return (and clear) the kernels' error word (0 = none)."""
+    """Synchronise `device` and return (and clear) the kernels' error word (0 = none). After an
+    error the cached GEMM workspaces of the device are dropped (their counters may be stale)."""
     code = ctypes.c_uint32(0)
     st = load().dsv32_device_status(device, ctypes.byref(code))
     if st not in (DSV32_OK, DSV32_ERR_DEVICE_TIMEOUT):
         check(st, "dsv32_device_status")
+    if code.value:
+        from . import kernels
+        for key in [k for k in kernels._GEMM_WS if k[0] == device]:
+            del kernels._GEMM_WS[key]
     return int(code.value)

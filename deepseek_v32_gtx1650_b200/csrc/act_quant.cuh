@@ -74,11 +74,16 @@ DSV32_DEV float aq_scale(float amax, bool round_scale) {
   return s;
 }
 
-DSV32_DEV int8_t aq_quant1(float x, float s) {
-  const float q = __fdiv_rn(x, s);  // IEEE division, as torch's g / s
-  int v = __float2int_rn(q);        // round half to even
-  v = max(-127, min(127, v));
-  return static_cast<int8_t>(v);
+// round_half_even(x / s) for |x| <= amax, s = amax-derived scale (|x / s| <= 127 + tiny).
+// Exact fast path: q = x * rcp_rn(s) is within 2^-15 of fl(x / s) for |q| < 128 (two correctly rounded
+// steps, 2^-23 relative), so rint(q) == rint(fl(x / s)) unless q lies within 2^-14 of a half
+// integer; those (about 1 in 8000) take the IEEE division. NaN converts to 0.
+DSV32_DEV int aq_quant1(float x, float s, float r) {
+  const float q = x * r;
+  const float n = rintf(q);
+  float v = n;
+  if (fabsf(q - n) > 0.5f - 6.103515625e-05f) v = rintf(__fdiv_rn(x, s));  // near a tie
+  return __float2int_rn(v);  // |v| <= 127: no clamp needed
 }
 
 template <typename T, int UNROLL>
@@ -133,21 +138,22 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
       float amax = fmaxf(a, 1e-4f);
       if (nan_lanes & group_lanes) amax = __int_as_float(0x7fc00000);
       const float sc = aq_scale(amax, round_scale != 0);
+      const float rc = __frcp_rn(sc);
       if (valid[u]) {
         const int64_t g = (base + u) * GPW + sub;
         if constexpr (EPL == 4) {
           char4 q;
-          q.x = aq_quant1(f[u][0], sc);
-          q.y = aq_quant1(f[u][1], sc);
-          q.z = aq_quant1(f[u][2], sc);
-          q.w = aq_quant1(f[u][3], sc);
+          q.x = static_cast<int8_t>(aq_quant1(f[u][0], sc, rc));
+          q.y = static_cast<int8_t>(aq_quant1(f[u][1], sc, rc));
+          q.z = static_cast<int8_t>(aq_quant1(f[u][2], sc, rc));
+          q.w = static_cast<int8_t>(aq_quant1(f[u][3], sc, rc));
           __stcs(reinterpret_cast<char4*>(y + g * 128) + sl, q);
         } else {
           uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) w0 |= (uint32_t(uint8_t(aq_quant1(f[u][e], sc))) << (8 * e));
+          for (int e = 0; e < 4; ++e) w0 |= (uint32_t(uint8_t(aq_quant1(f[u][e], sc, rc))) << (8 * e));
 #pragma unroll
-          for (int e = 0; e < 4; ++e) w1 |= (uint32_t(uint8_t(aq_quant1(f[u][4 + e], sc))) << (8 * e));
+          for (int e = 0; e < 4; ++e) w1 |= (uint32_t(uint8_t(aq_quant1(f[u][4 + e], sc, rc))) << (8 * e));
           __stcs(reinterpret_cast<uint2*>(y + g * 128) + sl, make_uint2(w0, w1));
         }
         if (sl == 0) s[g] = sc;

@@ -19,6 +19,8 @@
 
 namespace {
 
+constexpr int kAqUnroll = 4;  // 128-value groups in flight per warp slot per iteration
+
 thread_local std::string t_last_error;
 
 int cuda_fail(cudaError_t e, const char* what) {
@@ -38,6 +40,7 @@ struct DeviceInfo {
   bool ready = false;
   bool sm100 = false;
   int num_sms = 0;
+  int aq_blocks_per_sm[3] = {1, 1, 1};  // resident act_quant CTAs per SM, by input dtype
 };
 
 std::mutex g_mu;
@@ -67,12 +70,23 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<256, false>, gemm::Smem<256>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<256, true>, gemm::Smem<256>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<128, false>, gemm::Smem<128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<128, true>, gemm::Smem<128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128>, index::Cfg<64, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128>, index::Cfg<32, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128>, index::Cfg<16, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 64>, index::Cfg<64, 64>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 64>, index::Cfg<32, 64>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64>, index::Cfg<16, 64>::kAlloc));
+      {
+        int nb = 0;
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<float, kAqUnroll>, 256, 0));
+        d.aq_blocks_per_sm[DSV32_F32] = nb > 0 ? nb : 1;
+        DSV32_CUDA_TRY(
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__nv_bfloat16, kAqUnroll>, 256, 0));
+        d.aq_blocks_per_sm[DSV32_BF16] = nb > 0 ? nb : 1;
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__half, kAqUnroll>, 256, 0));
+        d.aq_blocks_per_sm[DSV32_F16] = nb > 0 ? nb : 1;
+      }
       if (!g_encode) {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -114,48 +128,89 @@ int launch_check(const char* what) {
   return DSV32_OK;
 }
 
-int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype, int64_t m,
-              int64_t n, int64_t k, int32_t* partials, void* stream) {
+struct GemmPlan {
+  int BN;
+  int64_t tiles, units;
+  int grid;
+  bool split;
+  int64_t ws_bytes;  // workspace the stream-K schedule needs (0 when data-parallel)
+};
+
+// Tile width and schedule for an (m, n, k) problem on this device. Stream-K only when there are
+// fewer tiles than SMs (decode-sized m): there it is the only way to use every SM. With at least a
+// wave of tiles, whole tiles per SM measured faster on B200 than splitting tiles (the partial-tile
+// round trip through the workspace costs more than the tail wave it removes).
+GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k, int num_sms) {
+  GemmPlan p;
+  p.BN = (n % 256 == 0) ? 256 : 128;
+  p.tiles = ((m + 127) / 128) * ((n + p.BN - 1) / p.BN);
+  p.units = p.tiles * (k / 128);
+  p.split = p.tiles < num_sms && p.tiles <= dsv32::gemm::kMaxSplitTiles;
+  if (p.split) {
+    p.grid = static_cast<int>(p.units < num_sms ? p.units : num_sms);
+    p.ws_bytes = (p.BN == 256) ? dsv32::gemm::workspace_bytes<256>(p.grid)
+                               : dsv32::gemm::workspace_bytes<128>(p.grid);
+  } else {
+    p.grid = static_cast<int>(p.tiles < num_sms ? p.tiles : num_sms);
+    p.ws_bytes = 0;
+  }
+  return p;
+}
+
+int gemm_check(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, const void* c, int c_dtype,
+               int64_t m, int64_t n, int64_t k) {
   if (!a || !a_s || !b || !b_s || !c) return DSV32_ERR_INVALID_ARG;
   if (m < 1 || n < 1 || k < 1) return DSV32_ERR_INVALID_ARG;
   if (k % 128 != 0 || n % 128 != 0) return DSV32_ERR_UNSUPPORTED;
   if (c_dtype != DSV32_F32 && c_dtype != DSV32_BF16 && c_dtype != DSV32_F16) return DSV32_ERR_INVALID_ARG;
   if (m > (1LL << 31) - 1 || n > (1LL << 31) - 1 || k > (1LL << 31) - 1) return DSV32_ERR_UNSUPPORTED;
   if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return DSV32_ERR_INVALID_ARG;
+  return DSV32_OK;
+}
+
+int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype, int64_t m,
+              int64_t n, int64_t k, int32_t* partials, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (int st = gemm_check(a, a_s, b, b_s, c, c_dtype, m, n, k)) return st;
+  if (workspace && !aligned16(workspace)) return DSV32_ERR_INVALID_ARG;
   int dev = 0;
   DeviceInfo* info = nullptr;
   if (int st = device_setup(&dev, &info)) return st;
 
-  // Narrow tiles when there are too few 128x256 tiles to cover the SMs, or N is an odd
-  // multiple of 128.
-  const int64_t tiles256 = ((m + 127) / 128) * ((n + 255) / 256);
-  const bool bn128 = !partials && ((n % 256) != 0 || tiles256 < info->num_sms);
-  const int BN = bn128 ? 128 : 256;
+  GemmPlan plan = gemm_plan(m, n, k, info->num_sms);
+  if (plan.split && (!workspace || workspace_bytes < plan.ws_bytes)) {
+    // No (large enough) workspace: data-parallel tiles.
+    plan.split = false;
+    plan.grid = static_cast<int>(plan.tiles < info->num_sms ? plan.tiles : info->num_sms);
+  }
+  uint8_t* ws = plan.split ? static_cast<uint8_t*>(workspace) : nullptr;
 
   CUtensorMap tmA, tmB;
   const uint64_t dimsA[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
   const uint64_t dimsB[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
   const uint64_t strides[1] = {static_cast<uint64_t>(k)};
   const uint32_t boxA[2] = {128, 128};
-  const uint32_t boxB[2] = {128, static_cast<uint32_t>(BN)};
+  const uint32_t boxB[2] = {128, static_cast<uint32_t>(plan.BN)};
   if (int st = encode_i8_map(&tmA, a, 2, dimsA, strides, boxA)) return st;
   if (int st = encode_i8_map(&tmB, b, 2, dimsB, strides, boxB)) return st;
 
-  const int64_t tiles = ((m + 127) / 128) * ((n + BN - 1) / BN);
-  const int grid = static_cast<int>(tiles < info->num_sms ? tiles : info->num_sms);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   using namespace dsv32::gemm;
-  if (partials) {
-    int8_gemm_kernel<256, true><<<grid, kThreads, Smem<256>::kAlloc, st>>>(
-        tmA, tmB, a_s, b_s, c, kOutF32, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), partials);
-  } else if (BN == 256) {
-    int8_gemm_kernel<256, false><<<grid, kThreads, Smem<256>::kAlloc, st>>>(
-        tmA, tmB, a_s, b_s, c, static_cast<uint32_t>(c_dtype), static_cast<int>(m), static_cast<int>(n),
-        static_cast<int>(k), nullptr);
+  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  const uint32_t ok = partials ? kOutF32 : static_cast<uint32_t>(c_dtype);
+  if (plan.BN == 256) {
+    if (partials)
+      int8_gemm_kernel<256, true><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                 ki, partials, ws);
+    else
+      int8_gemm_kernel<256, false><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                  ki, nullptr, ws);
   } else {
-    int8_gemm_kernel<128, false><<<grid, kThreads, Smem<128>::kAlloc, st>>>(
-        tmA, tmB, a_s, b_s, c, static_cast<uint32_t>(c_dtype), static_cast<int>(m), static_cast<int>(n),
-        static_cast<int>(k), nullptr);
+    if (partials)
+      int8_gemm_kernel<128, true><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                 ki, partials, ws);
+    else
+      int8_gemm_kernel<128, false><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                  ki, nullptr, ws);
   }
   return launch_check("int8_gemm_kernel launch");
 }
@@ -237,7 +292,7 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   } else if (n <= 512 * 16) {
     topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
   } else {
-    topk_radix_kernel<1024><<<g, 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+    topk_gmem_kernel<1024><<<g, 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
   }
   return launch_check("topk kernel launch");
 }
@@ -276,13 +331,14 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
   DeviceInfo* info = nullptr;
   if (int st = device_setup(&dev, &info)) return st;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  constexpr int kUnroll = 4;
+  constexpr int kUnroll = kAqUnroll;
   const int threads = 256;
   const int gpw = (x_dtype == DSV32_F32) ? 1 : 2;
   const int64_t slots = (groups + gpw - 1) / gpw;
   const int64_t warps_needed = (slots + kUnroll - 1) / kUnroll;
   int64_t blocks = (warps_needed + (threads / 32) - 1) / (threads / 32);
-  const int64_t cap = static_cast<int64_t>(info->num_sms) * 8;  // 8 resident CTAs per SM
+  // One wave of resident CTAs, each looping over its share: no tail wave.
+  const int64_t cap = static_cast<int64_t>(info->num_sms) * info->aq_blocks_per_sm[x_dtype];
   if (blocks > cap) blocks = cap;
   using namespace dsv32;
   if (x_dtype == DSV32_F32) {
@@ -299,14 +355,23 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
 }
 
 int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,
-                    int64_t m, int64_t n, int64_t k, void* stream) {
-  return gemm_impl(a, a_s, b, b_s, c, c_dtype, m, n, k, nullptr, stream);
+                    int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_impl(a, a_s, b, b_s, c, c_dtype, m, n, k, nullptr, workspace, workspace_bytes, stream);
+}
+
+int64_t dsv32_int8_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m < 1 || n < 1 || k < 1 || k % 128 != 0 || n % 128 != 0) return -DSV32_ERR_UNSUPPORTED;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return -st;
+  return gemm_plan(m, n, k, info->num_sms).ws_bytes;
 }
 
 int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, float* c,
-                             int32_t* partials, int64_t m, int64_t n, int64_t k, void* stream) {
+                             int32_t* partials, int64_t m, int64_t n, int64_t k, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
   if (!partials) return DSV32_ERR_INVALID_ARG;
-  return gemm_impl(a, a_s, b, b_s, c, DSV32_F32, m, n, k, partials, stream);
+  return gemm_impl(a, a_s, b, b_s, c, DSV32_F32, m, n, k, partials, workspace, workspace_bytes, stream);
 }
 
 int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,

@@ -7,17 +7,25 @@
 // A [M, K] int8 and B [N, K] int8 ("nn.Linear" layout), both K-contiguous, which is exactly
 // the K-major operand form tcgen05 reads; a_s [M, K/128], b_s [N/128, K/128] fp32.
 //
-// Design (one CTA per SM, persistent over 128 x BN output tiles):
+// Roles (one CTA per SM, 384 threads):
 //   warp 8      TMA producer: 128x128 A and BNx128 B tiles (SWIZZLE_128B) into a 4-stage ring.
 //   warp 9      MMA issuer: per 128-K block, 4 x tcgen05.mma.kind::i8 (K = 32 each) into one of
 //               two TMEM int32 accumulators (BN columns each), committed to the epilogue.
 //   warps 0-7   promotion epilogue: for every K block, tcgen05.ld the int32 partial, convert,
 //               multiply by a_s*b_s and accumulate in fp32 registers; refill the buffer with the
 //               conversion bias so the MMA of K block kb+2 can reuse it. Warp w owns TMEM lanes
-//               32*(w%4)..+31 (rows) and column half w/4.
+//               32*(w%4)..+31 (rows) and column half w/4. TMEM reads are software-pipelined:
+//               the next 32-column chunk is in flight while the current one is promoted.
 // The int32 partials are pre-biased (common.cuh: kI32FloatBiasBits): the accumulator starts at
 // bits(1.5*2^23), so after the MMA its bits read as the float 1.5*2^23 + partial, and a single
 // exact FADD recovers fp32(partial). |partial| <= 128*127*127 < 2^21, well inside the exact range.
+//
+// Schedule (stream-K): the work is tiles x K-blocks "units", ordered tile-major. CTA c processes
+// the contiguous unit range [U*c/G, U*(c+1)/G), so every SM gets the same number of K-blocks
+// whatever the tile count. A range covers whole tiles (stored directly) and at most two partial
+// tiles. A partial tile's fp32 accumulator goes to a workspace slot; the CTA that completes the
+// tile last (atomic counter) adds the slots in ascending K order and stores C. No CTA ever waits
+// for another. Without a workspace the kernel runs plain data-parallel tiles.
 //
 // Every mbarrier wait is bounded (common.cuh); on a timeout the CTA drains its in-flight TMA
 // loads and MMAs, frees TMEM and returns, leaving an error word for dsv32_device_status().
@@ -33,10 +41,10 @@ constexpr int kStages = 4;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 idle
 // Launch: 384 threads x 168 registers = 64512. setmaxnreg moves them to the epilogue:
-// 2 warpgroups x 128 x 232 + 1 warpgroup x 128 x 40 = 64512 (and per sub-partition
-// 232 + 232 + 40 = 504 <= 512).
-constexpr uint32_t kEpiRegs = 232;
-constexpr uint32_t kCtlRegs = 40;
+// 2 warpgroups x 128 x 216 + 1 warpgroup x 128 x 72 = 64512 (and per sub-partition
+// 216 + 216 + 72 = 504 <= 512).
+constexpr uint32_t kEpiRegs = 216;
+constexpr uint32_t kCtlRegs = 72;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 
@@ -53,9 +61,69 @@ struct Smem {
   static constexpr int kOffAbort = kOffTmem + 4;
   static constexpr int kBytes = kOffAbort + 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment (SWIZZLE_128B)
+  static constexpr int64_t kSlotFloats = int64_t(kBM) * BN;  // one partial tile, fp32
 };
 
 enum : uint32_t { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
+
+// Workspace layout (bytes): [counters: kMaxSplitTiles x 8 epilogue warps int32 (fixed size, so
+// the counters never share bytes with slot data whatever the problem shape)]
+// [2 * grid slots of kBM x BN fp32]. Slot 2c holds CTA c's first segment, slot 2c+1 its last one.
+// The counters must be zero before the first launch; every completed launch leaves them zero.
+constexpr int64_t kMaxSplitTiles = 65536;
+__host__ __device__ constexpr int64_t counter_bytes() { return kMaxSplitTiles * kEpiWarps * 4; }
+template <int BN>
+__host__ __device__ inline int64_t workspace_bytes(int grid) {
+  return counter_bytes() + int64_t(2) * grid * Smem<BN>::kSlotFloats * 4;
+}
+
+struct Sched {
+  int num_n, KG, num_tiles, grid;
+  long long U;  // total units = num_tiles * KG
+  bool split;   // stream-K (needs a workspace) or data-parallel tiles
+
+  DSV32_DEV long long ubeg(int c) const { return (U * c) / grid; }
+  DSV32_DEV int cta_of(long long u) const {
+    int c = static_cast<int>((u * grid) / U);
+    while (c + 1 < grid && ubeg(c + 1) <= u) ++c;
+    while (c > 0 && ubeg(c) > u) --c;
+    return c;
+  }
+};
+
+// Iterates this CTA's segments: (tile, kb0, kb1, first-segment flag).
+struct SegIter {
+  const Sched& s;
+  long long u, u1;  // stream-K range
+  int t;            // data-parallel tile cursor
+  bool first;
+  DSV32_DEV explicit SegIter(const Sched& sc) : s(sc), first(true) {
+    if (s.split) {
+      u = s.ubeg(blockIdx.x);
+      u1 = s.ubeg(blockIdx.x + 1);
+    } else {
+      t = blockIdx.x;
+    }
+  }
+  DSV32_DEV bool next(int& tile, int& kb0, int& kb1, bool& is_first) {
+    is_first = first;
+    first = false;
+    if (s.split) {
+      if (u >= u1) return false;
+      tile = static_cast<int>(u / s.KG);
+      kb0 = static_cast<int>(u % s.KG);
+      kb1 = static_cast<int>(min(static_cast<long long>(s.KG), kb0 + (u1 - u)));
+      u += kb1 - kb0;
+      return true;
+    }
+    if (t >= s.num_tiles) return false;
+    tile = t;
+    kb0 = 0;
+    kb1 = s.KG;
+    t += gridDim.x;
+    return true;
+  }
+};
 
 // Drain wait: bounded, ignores the abort flag (used only while winding down).
 DSV32_DEV void drain_wait(uint32_t bar, uint32_t parity) {
@@ -65,11 +133,68 @@ DSV32_DEV void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// acc[0..7] += (float(bits) - bias) * sc for 16 columns (8 float2 pairs).
+DSV32_DEV void promote16(const uint32_t (&r)[16], float2* acc, float2 sc2) {
+  const float2 nbias = make_float2(-kI32FloatBias, -kI32FloatBias);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float2 v = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+    v = __fadd2_rn(v, nbias);
+    acc[j] = __ffma2_rn(v, sc2, acc[j]);
+  }
+}
+
+// acc[0..15] += (float(bits) - bias) * sc for 32 columns (16 float2 pairs).
+DSV32_DEV void promote32(const uint32_t (&r)[32], float2* acc, float2 sc2) {
+  const float2 nbias = make_float2(-kI32FloatBias, -kI32FloatBias);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float2 v = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+    v = __fadd2_rn(v, nbias);
+    acc[j] = __ffma2_rn(v, sc2, acc[j]);
+  }
+}
+
+template <int kCols>
+DSV32_DEV void store_row(const float2 (&acc)[kCols / 2], void* C, uint32_t out_kind, int64_t off) {
+  if (out_kind == kOutF32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(C) + off);
+#pragma unroll
+    for (int j = 0; j < kCols / 4; ++j)
+      dst[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+  } else if (out_kind == kOutBF16) {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(C) + off);
+#pragma unroll
+    for (int j = 0; j < kCols / 8; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h = __float22bfloat162_rn(acc[4 * j + i]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(C) + off);
+#pragma unroll
+    for (int j = 0; j < kCols / 8; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __half2 h = __float22half2_rn(acc[4 * j + i]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
 template <int BN, bool kPartials>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ a_s, const float* __restrict__ b_s, void* __restrict__ C,
-                     uint32_t out_kind, int M, int N, int K, int32_t* __restrict__ partials) {
+                     uint32_t out_kind, int M, int N, int K, int32_t* __restrict__ partials,
+                     uint8_t* __restrict__ workspace) {
   using L = Smem<BN>;
   constexpr int kCols = BN / 2;  // columns per epilogue thread
   extern __shared__ uint8_t smem_raw[];
@@ -90,10 +215,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int KG = K / kBK;
-  const int num_m = (M + kBM - 1) / kBM;
-  const int num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  Sched sch;
+  sch.KG = K / kBK;
+  sch.num_n = (N + BN - 1) / BN;
+  sch.num_tiles = ((M + kBM - 1) / kBM) * sch.num_n;
+  sch.grid = gridDim.x;
+  sch.U = static_cast<long long>(sch.num_tiles) * sch.KG;
+  sch.split = workspace != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -125,10 +253,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t / num_n) * kBM;
-        const int n0 = (t % num_n) * BN;
-        for (int kb = 0; kb < KG; ++kb) {
+      SegIter it(sch);
+      int tile, kb0, kb1;
+      bool first;
+      while (ok && it.next(tile, kb0, kb1, first)) {
+        const int m0 = (tile / sch.num_n) * kBM;
+        const int n0 = (tile % sch.num_n) * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, (KID_GEMM << 16) | 1)) {
             ok = false;
             break;
@@ -159,8 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t u = 0;  // K blocks processed by this CTA (selects the TMEM buffer)
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        for (int kb = 0; kb < KG; ++kb, ++u) {
+      SegIter it(sch);
+      int tile, kb0, kb1;
+      bool first;
+      while (ok && it.next(tile, kb0, kb1, first)) {
+        for (int kb = kb0; kb < kb1; ++kb, ++u) {
           const uint32_t buf = u & 1u;
           if (!mbar_wait(tempty_bar(buf), (u >> 1) & 1u, abort_flag, (KID_GEMM << 16) | 2) ||
               !mbar_wait(full_bar(stage), phase, abort_flag, (KID_GEMM << 16) | 3)) {
@@ -191,7 +325,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ promotion epilogue
     const int wq = warp & 3;   // TMEM lane quarter
     const int wh = warp >> 2;  // column half
+    const int r_local = wq * 32 + lane;  // row within the tile
     const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wh * kCols);
+    int* counters = reinterpret_cast<int*>(workspace);
+    float* slots = workspace ? reinterpret_cast<float*>(workspace + counter_bytes()) : nullptr;
     bool ok = true;
     // Arm both accumulators with the conversion bias.
 #pragma unroll
@@ -207,50 +344,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(tempty_bar(1));
     }
     uint32_t u = 0;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const int m0 = (t / num_n) * kBM;
-      const int n0 = (t % num_n) * BN;
-      const int row = m0 + wq * 32 + lane;
+    SegIter it(sch);
+    int tile, kb0, kb1;
+    bool first_seg;
+    while (ok && it.next(tile, kb0, kb1, first_seg)) {
+      const int m0 = (tile / sch.num_n) * kBM;
+      const int n0 = (tile % sch.num_n) * BN;
+      const int row = m0 + r_local;
       const int col0 = n0 + wh * kCols;
       const bool row_ok = row < M;
       const bool cols_ok = col0 < N;  // N % 128 == 0: a half is either fully in or fully out
-      const float* as_row = a_s + static_cast<int64_t>(row_ok ? row : 0) * KG;
-      const float* bs_row = b_s + static_cast<int64_t>(cols_ok ? (col0 / 128) : 0) * KG;
+      const float* as_row = a_s + static_cast<int64_t>(row_ok ? row : 0) * sch.KG;
+      const float* bs_row = b_s + static_cast<int64_t>(cols_ok ? (col0 / 128) : 0) * sch.KG;
       float2 acc[kCols / 2];
 #pragma unroll
       for (int j = 0; j < kCols / 2; ++j) acc[j] = make_float2(0.f, 0.f);
 
-      for (int kb = 0; kb < KG; ++kb, ++u) {
+      float sa_next = row_ok ? __ldg(as_row + kb0) : 0.f;
+      float sb_next = cols_ok ? __ldg(bs_row + kb0) : 0.f;
+      for (int kb = kb0; kb < kb1; ++kb, ++u) {
         const uint32_t buf = u & 1u;
-        const float sa = row_ok ? __ldg(as_row + kb) : 0.f;
-        const float sb = cols_ok ? __ldg(bs_row + kb) : 0.f;
-        const float sc = sa * sb;
+        const float sc = sa_next * sb_next;
+        if (kb + 1 < kb1) {  // prefetch the next block's scales
+          sa_next = row_ok ? __ldg(as_row + kb + 1) : 0.f;
+          sb_next = cols_ok ? __ldg(bs_row + kb + 1) : 0.f;
+        }
         const float2 sc2 = make_float2(sc, sc);
-        const float2 nbias = make_float2(-kI32FloatBias, -kI32FloatBias);
         if (!mbar_wait_warp(tfull_bar(buf), (u >> 1) & 1u, abort_flag, (KID_GEMM << 16) | 4)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t tb = t_lane + buf * BN;
+        constexpr int kCW = 16;  // columns per TMEM read
+        uint32_t ra[kCW], rb[kCW];
+        tmem_ld16_async(tb, ra);
+        tmem_wait_ld16(ra);
 #pragma unroll
-        for (int c = 0; c < kCols / 32; ++c) {
-          uint32_t r[32];
-          const uint32_t ta = t_lane + buf * BN + c * 32;
-          tmem_ld32(ta, r);
-          tmem_fill32(ta, kI32FloatBiasBits);
+        for (int c = 0; c < kCols / kCW; ++c) {
+          uint32_t(&cur)[kCW] = (c & 1) ? rb : ra;
+          uint32_t(&nxt)[kCW] = (c & 1) ? ra : rb;
+          if (c + 1 < kCols / kCW) tmem_ld16_async(tb + (c + 1) * kCW, nxt);  // in flight during promote
+          tmem_fill16(tb + c * kCW, kI32FloatBiasBits);                        // re-arm the finished chunk
           if constexpr (kPartials) {
             if (row_ok && cols_ok) {
-              int32_t* p = partials + (static_cast<int64_t>(kb) * M + row) * N + col0 + c * 32;
+              int32_t* p = partials + (static_cast<int64_t>(kb) * M + row) * N + col0 + c * kCW;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) p[j] = static_cast<int32_t>(r[j] - kI32FloatBiasBits);
+              for (int j = 0; j < kCW; ++j) p[j] = static_cast<int32_t>(cur[j] - kI32FloatBiasBits);
             }
           }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float2 v = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-            v = __fadd2_rn(v, nbias);
-            acc[c * 16 + j] = __ffma2_rn(v, sc2, acc[c * 16 + j]);
-          }
+          promote16(cur, acc + c * (kCW / 2), sc2);
+          if (c + 1 < kCols / kCW) tmem_wait_ld16(nxt);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -258,39 +402,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(tempty_bar(buf));
       }
       if (!ok) break;
+
+      const bool full_tile = (kb0 == 0 && kb1 == sch.KG);
+      const int64_t off = static_cast<int64_t>(row) * N + col0;
+      if (full_tile) {
+        if (row_ok && cols_ok) store_row<kCols>(acc, C, out_kind, off);
+        continue;
+      }
+      // Partial tile: publish this warp's 32 rows x kCols of the segment; the warp that completes
+      // this sub-tile last (one counter per tile and warp) reduces and stores. Warp-local: no
+      // barrier across warps, so an aborting warp can never strand the others.
+      const int slot = 2 * blockIdx.x + (first_seg ? 0 : 1);
+      float* my_slot = slots + slot * L::kSlotFloats + static_cast<int64_t>(wh) * kCols * kBM;
       if (row_ok && cols_ok) {
-        const int64_t off = static_cast<int64_t>(row) * N + col0;
-        if (out_kind == kOutF32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(C) + off);
 #pragma unroll
-          for (int j = 0; j < kCols / 4; ++j)
-            dst[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
-        } else if (out_kind == kOutBF16) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(C) + off);
-#pragma unroll
-          for (int j = 0; j < kCols / 8; ++j) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              __nv_bfloat162 h = __float22bfloat162_rn(acc[4 * j + i]);
-              w[i] = *reinterpret_cast<uint32_t*>(&h);
-            }
-            dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(C) + off);
-#pragma unroll
-          for (int j = 0; j < kCols / 8; ++j) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              __half2 h = __float22half2_rn(acc[4 * j + i]);
-              w[i] = *reinterpret_cast<uint32_t*>(&h);
-            }
-            dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
-          }
+        for (int j = 0; j < kCols / 2; ++j) {  // column-major slot: lanes write consecutive rows
+          __stcg(my_slot + (2 * j) * kBM + r_local, acc[j].x);
+          __stcg(my_slot + (2 * j + 1) * kBM + r_local, acc[j].y);
         }
       }
+      __threadfence();
+      __syncwarp();
+      const long long t_u0 = static_cast<long long>(tile) * sch.KG;
+      const int c_first = sch.cta_of(t_u0);
+      const int c_last = sch.cta_of(t_u0 + sch.KG - 1);
+      int is_last = 0;
+      if (lane == 0) {
+        int* ctr = counters + static_cast<int64_t>(tile) * kEpiWarps + warp;
+        const int prev = atomicAdd(ctr, 1);
+        is_last = (prev == c_last - c_first);
+        if (is_last) *ctr = 0;  // ready for the next launch
+      }
+      is_last = __shfl_sync(0xffffffffu, is_last, 0);
+      if (!is_last) continue;
+      __threadfence();
+      if (!(row_ok && cols_ok)) continue;
+      // Every contributor (this one included) has written its slot: sum them in ascending K order
+      // so the result does not depend on which CTA arrived last.
+#pragma unroll
+      for (int j = 0; j < kCols / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+      for (int cc = c_first; cc <= c_last; ++cc) {
+        const int first_tile_of_cc = static_cast<int>(sch.ubeg(cc) / sch.KG);
+        const int s = 2 * cc + (first_tile_of_cc == tile ? 0 : 1);
+        const float* ps = slots + s * L::kSlotFloats + static_cast<int64_t>(wh) * kCols * kBM;
+#pragma unroll
+        for (int j = 0; j < kCols / 2; ++j) {
+          const float2 v = make_float2(__ldcg(ps + (2 * j) * kBM + r_local), __ldcg(ps + (2 * j + 1) * kBM + r_local));
+          acc[j] = __fadd2_rn(acc[j], v);
+        }
+      }
+      store_row<kCols>(acc, C, out_kind, off);
     }
   }
 

@@ -250,12 +250,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         float2 acc[C::kQPerHalf];
 #pragma unroll
         for (int q = 0; q < C::kQPerHalf; ++q) acc[q] = make_float2(0.f, 0.f);
+        // TMEM reads are software-pipelined: chunk c+1 is in flight while chunk c is reduced.
+        const uint32_t tb = t_lane + buf * kNmma;
+        uint32_t ra[32], rb[32];
+        tmem_ld32_async(tb, ra);
+        tmem_wait_ld32(ra);
 #pragma unroll
         for (int c = 0; c < C::kColsPerHalf / 32; ++c) {
-          uint32_t r[32];
-          const uint32_t ta = t_lane + buf * kNmma + c * 32;
-          tmem_ld32(ta, r);
-          tmem_fill32(ta, kI32FloatBiasBits);
+          uint32_t(&r)[32] = (c & 1) ? rb : ra;
+          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+          if (c + 1 < C::kColsPerHalf / 32) tmem_ld32_async(tb + (c + 1) * 32, nxt);
+          tmem_fill32(tb + c * 32, kI32FloatBiasBits);  // re-arm the finished chunk
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
             const float4 w4 = w_half[c * 8 + j4];  // same address across the warp: broadcast
@@ -271,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc[q] = __ffma2_rn(v, wv, acc[q]);
             }
           }
+          if (c + 1 < C::kColsPerHalf / 32) tmem_wait_ld32(nxt);
         }
         tmem_wait_st();
         tc_fence_before();

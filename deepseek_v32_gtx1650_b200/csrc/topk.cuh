@@ -8,32 +8,49 @@
 // so "lower position" is "lower global key index", and the merge of per-shard top-k lists
 // reproduces the single-GPU selection exactly.
 //
-// Values are mapped to order-preserving uint32 keys (larger float -> larger key, -inf is
-// the smallest finite-or-masked key), so every comparison is an integer comparison.
-//
-// Two kernels:
-//   topk_reg_kernel   rows of n <= THREADS*ITEMS: keys live in registers; the k-th key is found
-//                     by a 32-step bisection over key bits (block-wide counts, no atomics).
-//   topk_radix_kernel any n: three radix-histogram passes (11/11/10 bits) over the row in
-//                     global memory (smem histogram), then the same ordered compaction.
+// Algorithm (radix select on order-preserving uint32 keys; larger float -> larger key):
+//  1. Block reductions give the number of finite values and the min / max finite key. Masked
+//     (-inf) scores never enter a histogram: when at most k values are finite, the threshold is
+//     the -inf key itself and the lowest-position masked keys fill the list.
+//  2. Otherwise the bits above the highest bit in which min and max differ are common to every
+//     finite key; the remaining bits are resolved with 11-bit shared-memory histograms (at most
+//     three passes), each pass counting only keys that match the prefix found so far.
+//  3. Ordered compaction: block-wide prefix sums over per-thread contiguous chunks place every
+//     key > T and the first k_rem keys == T in position order.
+// topk_reg_kernel keeps a row of up to THREADS*ITEMS keys in registers (one read of the row);
+// topk_gmem_kernel re-reads longer rows from global memory (L2) in each pass.
 #pragma once
 #include "common.cuh"
 
 namespace dsv32 {
 namespace topk {
 
+constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // key of -inf: below every finite value
+constexpr int kHistBits = 11;
+
 DSV32_DEV uint32_t fkey(float f) {
   const uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Block-wide sum; `scratch` holds 2 * (THREADS/32) ints and `parity` alternates between calls
-// so one __syncthreads per call suffices.
+DSV32_DEV float fkey_inv(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+  return __uint_as_float(u);
+}
+
+// Keys of a row fall into: "above" (> the -inf key: finite, +inf, +NaN), the -inf key, and
+// below it (negative NaN). Masked -inf entries are counted, never histogrammed.
+DSV32_DEV bool prefix_match(uint32_t key, uint32_t prefix, int shift) {
+  return shift >= 32 || (key >> shift) == (prefix >> shift);
+}
+
+// Block-wide sum / min / max; `scratch` holds 2 * 32 ints and `parity` alternates so one
+// __syncthreads per call suffices.
 template <int THREADS>
 DSV32_DEV int block_sum(int v, int* scratch, int& parity) {
   constexpr int W = THREADS / 32;
   v = __reduce_add_sync(0xffffffffu, v);
-  int* buf = scratch + parity * W;
+  int* buf = scratch + parity * 32;
   if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = v;
   __syncthreads();
   int s = 0;
@@ -43,9 +60,30 @@ DSV32_DEV int block_sum(int v, int* scratch, int& parity) {
   return s;
 }
 
+template <int THREADS>
+DSV32_DEV void block_minmax(uint32_t& mn, uint32_t& mx, uint32_t* scratch, int& parity) {
+  constexpr int W = THREADS / 32;
+  mn = __reduce_min_sync(0xffffffffu, mn);
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  uint32_t* buf = scratch + parity * 64;
+  if ((threadIdx.x & 31) == 0) {
+    buf[threadIdx.x >> 5] = mn;
+    buf[32 + (threadIdx.x >> 5)] = mx;
+  }
+  __syncthreads();
+  mn = 0xFFFFFFFFu;
+  mx = 0u;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    mn = min(mn, buf[i]);
+    mx = max(mx, buf[32 + i]);
+  }
+  parity ^= 1;
+}
+
 // Block-wide exclusive prefix sum in thread order.
 template <int THREADS>
-DSV32_DEV int block_excl_scan(int v, int* scratch, int& parity, int* total = nullptr) {
+DSV32_DEV int block_excl_scan(int v, int* scratch, int& parity) {
   constexpr int W = THREADS / 32;
   const int lane = threadIdx.x & 31;
   int incl = v;
@@ -54,78 +92,129 @@ DSV32_DEV int block_excl_scan(int v, int* scratch, int& parity, int* total = nul
     const int t = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += t;
   }
-  int* buf = scratch + parity * W;
+  int* buf = scratch + parity * 32;
   if (lane == 31) buf[threadIdx.x >> 5] = incl;
   __syncthreads();
-  int before = 0, all = 0;
+  int before = 0;
   const int wid = threadIdx.x >> 5;
 #pragma unroll
-  for (int i = 0; i < W; ++i) {
-    const int t = buf[i];
-    before += (i < wid) ? t : 0;
-    all += t;
-  }
+  for (int i = 0; i < W; ++i) before += (i < wid) ? buf[i] : 0;
   parity ^= 1;
-  if (total) *total = all;
   return before + incl - v;
 }
 
-// Selected outputs of one thread's contiguous chunk, in position order.
-template <int ITEMS>
-DSV32_DEV void emit_chunk(const uint32_t (&key)[ITEMS], const float (&val)[ITEMS], int pos0, int n, uint32_t T,
-                          int eq_before, int k_rem, int out_base, const int32_t* cand_row, long long idx_offset,
-                          int32_t* out_idx_row, float* out_val_row) {
-  int o = out_base;
-  int eq = eq_before;
-#pragma unroll
-  for (int i = 0; i < ITEMS; ++i) {
-    const int pos = pos0 + i;
-    if (pos < n) {
-      bool sel = key[i] > T;
-      if (key[i] == T) {
-        sel = eq < k_rem;
-        ++eq;
+// Shared state of one selection.
+struct SelShared {
+  int hist[1 << kHistBits];
+  int scratch[64];
+  uint32_t mm[128];
+  uint32_t prefix;
+  int krem;
+};
+
+// After a histogram over digit bits [shift, shift + d), find the digit of the k_rem-th largest
+// participating key. Updates prefix / k_rem in shared memory (all threads read them after).
+template <int THREADS>
+DSV32_DEV void pick_digit(SelShared& sh, int nbins, int shift, uint32_t prefix, int k_rem, int& parity) {
+  const int per = (nbins + THREADS - 1) / THREADS;  // bins per thread, descending order
+  int local = 0;
+  for (int j = 0; j < per; ++j) {
+    const int bin = nbins - 1 - (threadIdx.x * per + j);
+    if (bin >= 0) local += sh.hist[bin];
+  }
+  const int before = block_excl_scan<THREADS>(local, sh.scratch, parity);
+  if (before < k_rem && k_rem <= before + local) {
+    int acc = before;
+    for (int j = 0; j < per; ++j) {
+      const int bin = nbins - 1 - (threadIdx.x * per + j);
+      const int c = sh.hist[bin];
+      if (acc + c >= k_rem) {
+        sh.prefix = prefix | (uint32_t(bin) << shift);
+        sh.krem = k_rem - acc;
+        break;
       }
-      if (sel) {
-        out_idx_row[o] = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + idx_offset);
-        out_val_row[o] = val[i];
-        ++o;
-      }
+      acc += c;
     }
   }
+  __syncthreads();
 }
 
+// ---------------------------------------------------------------------------- register rows
 template <int THREADS, int ITEMS>
 __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restrict__ vals, long long ld, int n,
                                                            const int32_t* __restrict__ cand_idx, long long cand_ld,
                                                            long long idx_offset, int k, int32_t* __restrict__ out_idx,
                                                            float* __restrict__ out_val) {
-  __shared__ int scratch[2 * (THREADS / 32)];
+  __shared__ SelShared sh;
   int parity = 0;
   const long long row = blockIdx.x;
   const float* v = vals + row * ld;
   const int pos0 = threadIdx.x * ITEMS;
   uint32_t key[ITEMS];
-  float val[ITEMS];
+  // Each thread owns ITEMS consecutive positions (position order = thread order).
+  if ((ld & 3) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && (ITEMS % 4) == 0 && pos0 + ITEMS <= n) {
+#pragma unroll
+    for (int i = 0; i < ITEMS; i += 4) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(v + pos0 + i));
+      key[i] = fkey(f.x);
+      key[i + 1] = fkey(f.y);
+      key[i + 2] = fkey(f.z);
+      key[i + 3] = fkey(f.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) key[i] = (pos0 + i < n) ? fkey(__ldg(v + pos0 + i)) : 0u;
+  }
+  // 1. counts above / at the -inf key; range of the keys that take part in the histograms
+  int n_above = 0, n_ninf = 0;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
-    const int pos = pos0 + i;
-    val[i] = (pos < n) ? v[pos] : -INFINITY;
-    key[i] = (pos < n) ? fkey(val[i]) : 0u;
+    const bool valid = pos0 + i < n;
+    n_above += (valid && key[i] > kNegInfKey) ? 1 : 0;
+    n_ninf += (valid && key[i] == kNegInfKey) ? 1 : 0;
   }
-  int valid = 0;
+  const int above = block_sum<THREADS>(n_above, sh.scratch, parity);
+  const int ninf = block_sum<THREADS>(n_ninf, sh.scratch, parity);
+  uint32_t T;
+  int k_rem;
+  if (above < k && above + ninf >= k) {
+    T = kNegInfKey;  // all values above -inf, then the lowest-position -inf entries
+    k_rem = k - above;
+  } else {
+    // 2. radix select among keys >= floor (above -inf; or every key if negative NaNs are needed)
+    const uint32_t floor_key = (above >= k) ? kNegInfKey + 1u : 0u;
+    uint32_t mn = 0xFFFFFFFFu, mx = 0u;
 #pragma unroll
-  for (int i = 0; i < ITEMS; ++i) valid += (pos0 + i < n) ? 1 : 0;
-
-  // Largest T with count(key >= T) >= k, bit by bit from the top.
-  uint32_t T = 0;
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = T | (1u << bit);
-    int c = 0;
+    for (int i = 0; i < ITEMS; ++i) {
+      const bool part = pos0 + i < n && key[i] >= floor_key;
+      mn = part ? min(mn, key[i]) : mn;
+      mx = part ? max(mx, key[i]) : mx;
+    }
+    block_minmax<THREADS>(mn, mx, sh.mm, parity);
+    int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);  // bits [shift, 32) common to every participant
+    uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
+    k_rem = k;
+    while (shift > 0) {
+      const int d = min(kHistBits, shift);
+      const int nbins = 1 << d;
+      for (int i = threadIdx.x; i < nbins; i += THREADS) sh.hist[i] = 0;
+      __syncthreads();
+      const int ns = shift - d;
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) c += (pos0 + i < n && key[i] >= cand) ? 1 : 0;
-    if (block_sum<THREADS>(c, scratch, parity) >= k) T = cand;
+      for (int i = 0; i < ITEMS; ++i) {
+        const bool part = pos0 + i < n && key[i] >= floor_key && prefix_match(key[i], prefix, shift);
+        if (part) atomicAdd(&sh.hist[(key[i] >> ns) & (nbins - 1)], 1);
+      }
+      __syncthreads();
+      pick_digit<THREADS>(sh, nbins, ns, prefix, k_rem, parity);
+      prefix = sh.prefix;
+      k_rem = sh.krem;
+      shift = ns;
+      __syncthreads();
+    }
+    T = prefix;
   }
+  // 3. ordered compaction
   int gt = 0, eq = 0;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
@@ -134,93 +223,104 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
       eq += key[i] == T ? 1 : 0;
     }
   }
-  (void)valid;
-  const int G = block_sum<THREADS>(gt, scratch, parity);
-  const int k_rem = k - G;  // ties at T to take, lowest positions first
-  const int eq_before = block_excl_scan<THREADS>(eq, scratch, parity);
+  const int eq_before = block_excl_scan<THREADS>(eq, sh.scratch, parity);
   const int take_eq = max(0, min(eq, k_rem - eq_before));
-  const int out_base = block_excl_scan<THREADS>(gt + take_eq, scratch, parity);
-  emit_chunk<ITEMS>(key, val, pos0, n, T, eq_before, k_rem, out_base, cand_idx ? cand_idx + row * cand_ld : nullptr,
-                    idx_offset, out_idx + row * k, out_val + row * k);
+  int o = block_excl_scan<THREADS>(gt + take_eq, sh.scratch, parity);
+  const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld : nullptr;
+  int32_t* oi = out_idx + row * k;
+  float* ov = out_val + row * k;
+  int e = eq_before;
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    const int pos = pos0 + i;
+    if (pos < n) {
+      bool sel = key[i] > T;
+      if (key[i] == T) {
+        sel = e < k_rem;
+        ++e;
+      }
+      if (sel) {
+        oi[o] = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + idx_offset);
+        ov[o] = fkey_inv(key[i]);
+        ++o;
+      }
+    }
+  }
 }
 
-// Generic version for long rows: radix histogram passes over global memory.
+// ---------------------------------------------------------------------------- long rows
 template <int THREADS>
-__global__ void __launch_bounds__(THREADS) topk_radix_kernel(const float* __restrict__ vals, long long ld, int n,
-                                                             const int32_t* __restrict__ cand_idx, long long cand_ld,
-                                                             long long idx_offset, int k, int32_t* __restrict__ out_idx,
-                                                             float* __restrict__ out_val) {
-  constexpr int kBins = 2048;
-  __shared__ int hist[kBins];
-  __shared__ int scratch[2 * (THREADS / 32)];
-  __shared__ uint32_t s_prefix;
-  __shared__ int s_krem;
+__global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restrict__ vals, long long ld, int n,
+                                                            const int32_t* __restrict__ cand_idx, long long cand_ld,
+                                                            long long idx_offset, int k, int32_t* __restrict__ out_idx,
+                                                            float* __restrict__ out_val) {
+  __shared__ SelShared sh;
   int parity = 0;
   const long long row = blockIdx.x;
   const float* v = vals + row * ld;
-
-  uint32_t prefix = 0, pmask = 0;
-  int k_rem = k;
-  const int shifts[3] = {21, 10, 0};
-  const int widths[3] = {11, 11, 10};
-  for (int p = 0; p < 3; ++p) {
-    const int nb = 1 << widths[p];
-    for (int i = threadIdx.x; i < nb; i += THREADS) hist[i] = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += THREADS) {
-      const uint32_t kk = fkey(v[i]);
-      if ((kk & pmask) == prefix) atomicAdd(&hist[(kk >> shifts[p]) & (nb - 1)], 1);
-    }
-    __syncthreads();
-    // Walk bins from the top: per-thread contiguous bin groups in descending order.
-    constexpr int kPer = kBins / THREADS > 0 ? kBins / THREADS : 1;
-    const int per = (nb + THREADS - 1) / THREADS;
-    int local = 0;
-    for (int j = 0; j < per; ++j) {
-      const int bin = nb - 1 - (threadIdx.x * per + j);
-      if (bin >= 0) local += hist[bin];
-    }
-    (void)kPer;
-    const int before = block_excl_scan<THREADS>(local, scratch, parity);
-    if (before < k_rem && k_rem <= before + local) {
-      int acc = before;
-      for (int j = 0; j < per; ++j) {
-        const int bin = nb - 1 - (threadIdx.x * per + j);
-        const int c = hist[bin];
-        if (acc + c >= k_rem) {
-          s_prefix = prefix | (uint32_t(bin) << shifts[p]);
-          s_krem = k_rem - acc;
-          break;
-        }
-        acc += c;
-      }
-    }
-    __syncthreads();
-    prefix = s_prefix;
-    k_rem = s_krem;
-    pmask |= uint32_t(nb - 1) << shifts[p];
-    __syncthreads();
+  int n_above = 0, n_ninf = 0;
+  for (int i = threadIdx.x; i < n; i += THREADS) {
+    const uint32_t kk = fkey(__ldg(v + i));
+    n_above += kk > kNegInfKey ? 1 : 0;
+    n_ninf += kk == kNegInfKey ? 1 : 0;
   }
-  const uint32_t T = prefix;
+  const int above = block_sum<THREADS>(n_above, sh.scratch, parity);
+  const int ninf = block_sum<THREADS>(n_ninf, sh.scratch, parity);
+  uint32_t T;
+  int k_rem;
+  if (above < k && above + ninf >= k) {
+    T = kNegInfKey;
+    k_rem = k - above;
+  } else {
+    const uint32_t floor_key = (above >= k) ? kNegInfKey + 1u : 0u;
+    uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+    for (int i = threadIdx.x; i < n; i += THREADS) {
+      const uint32_t kk = fkey(__ldg(v + i));
+      mn = kk >= floor_key ? min(mn, kk) : mn;
+      mx = kk >= floor_key ? max(mx, kk) : mx;
+    }
+    block_minmax<THREADS>(mn, mx, sh.mm, parity);
+    int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);
+    uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
+    k_rem = k;
+    while (shift > 0) {
+      const int d = min(kHistBits, shift);
+      const int nbins = 1 << d;
+      for (int i = threadIdx.x; i < nbins; i += THREADS) sh.hist[i] = 0;
+      __syncthreads();
+      const int ns = shift - d;
+      for (int i = threadIdx.x; i < n; i += THREADS) {
+        const uint32_t kk = fkey(__ldg(v + i));
+        if (kk >= floor_key && prefix_match(kk, prefix, shift)) atomicAdd(&sh.hist[(kk >> ns) & (nbins - 1)], 1);
+      }
+      __syncthreads();
+      pick_digit<THREADS>(sh, nbins, ns, prefix, k_rem, parity);
+      prefix = sh.prefix;
+      k_rem = sh.krem;
+      shift = ns;
+      __syncthreads();
+    }
+    T = prefix;
+  }
   // Ordered compaction over per-thread contiguous chunks.
   const int chunk = (n + THREADS - 1) / THREADS;
   const int p0 = threadIdx.x * chunk;
   const int p1 = min(n, p0 + chunk);
   int gt = 0, eq = 0;
   for (int pos = p0; pos < p1; ++pos) {
-    const uint32_t kk = fkey(v[pos]);
+    const uint32_t kk = fkey(__ldg(v + pos));
     gt += kk > T;
     eq += kk == T;
   }
-  const int eq_before = block_excl_scan<THREADS>(eq, scratch, parity);
+  const int eq_before = block_excl_scan<THREADS>(eq, sh.scratch, parity);
   const int take_eq = max(0, min(eq, k_rem - eq_before));
-  int o = block_excl_scan<THREADS>(gt + take_eq, scratch, parity);
+  int o = block_excl_scan<THREADS>(gt + take_eq, sh.scratch, parity);
   const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld : nullptr;
   int32_t* oi = out_idx + row * k;
   float* ov = out_val + row * k;
   int e = eq_before;
   for (int pos = p0; pos < p1; ++pos) {
-    const float x = v[pos];
+    const float x = __ldg(v + pos);
     const uint32_t kk = fkey(x);
     bool sel = kk > T;
     if (kk == T) {

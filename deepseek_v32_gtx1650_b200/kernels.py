@@ -23,6 +23,40 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+class _OnDevice:
+    """Make t's device current for the library call (a no-op when it already is)."""
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.prev)
+
+
+# GEMM workspace per (device, stream): zero-filled once, left reusable by every launch. Keyed by
+# stream because two launches sharing one workspace must not overlap on the GPU.
+_GEMM_WS: dict = {}
+
+
+def _gemm_workspace(dev: torch.device, stream: int, M: int, N: int, K: int):
+    nbytes = int(_lib.load().dsv32_int8_gemm_workspace_bytes(M, N, K))
+    if nbytes <= 0:
+        return None, 0
+    key = (dev.index, stream)
+    ws = _GEMM_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _GEMM_WS[key] = ws
+    return ws.data_ptr(), ws.numel()
+
+
 def _require_cuda(*ts: torch.Tensor) -> None:
     for t in ts:
         if not t.is_cuda:
@@ -41,7 +75,7 @@ def act_quant(x: torch.Tensor, round_scale: bool = False, block_m: int = 32):
     y = torch.empty_like(x2, dtype=torch.int8)
     s = torch.empty(M, NG, device=x.device, dtype=torch.float32)
     if M > 0 and N > 0:
-        with torch.cuda.device(x.device):
+        with _OnDevice(x):
             _lib.check(_lib.load().dsv32_act_quant(x2.data_ptr(), _DT[x.dtype], M, N, int(bool(round_scale)),
                                                    y.data_ptr(), s.data_ptr(), _stream(x)), "act_quant")
     return y.view(x.shape), s.view(*x.shape[:-1], NG)
@@ -63,9 +97,11 @@ def int8_gemm(a, a_s, b, b_s, out_dtype=torch.float32, version="v1"):
     _require_cuda(a, a_s, b, b_s)
     c = torch.empty(*a.shape[:-1], N, device=a.device, dtype=out_dtype)
     if M > 0 and N > 0 and K > 0:
-        with torch.cuda.device(a.device):
+        with _OnDevice(a):
+            st = _stream(a)
+            ws, wsb = _gemm_workspace(a.device, st, M, N, K)
             _lib.check(_lib.load().dsv32_int8_gemm(a.data_ptr(), a_s.data_ptr(), b.data_ptr(), b_s.data_ptr(),
-                                                   c.data_ptr(), _DT[out_dtype], M, N, K, _stream(a)), "int8_gemm")
+                                                   c.data_ptr(), _DT[out_dtype], M, N, K, ws, wsb, st), "int8_gemm")
     return c
 
 
@@ -80,9 +116,11 @@ def int8_gemm_partials(a, a_s, b, b_s):
     _require_cuda(a, a_s, b, b_s)
     c = torch.empty(M, N, device=a.device, dtype=torch.float32)
     p = torch.empty(K // GROUP, M, N, device=a.device, dtype=torch.int32)
-    with torch.cuda.device(a.device):
+    with _OnDevice(a):
+        st = _stream(a)
+        ws, wsb = _gemm_workspace(a.device, st, M, N, K)
         _lib.check(_lib.load().dsv32_int8_gemm_partials(a.data_ptr(), a_s.data_ptr(), b.data_ptr(), b_s.data_ptr(),
-                                                        c.data_ptr(), p.data_ptr(), M, N, K, _stream(a)),
+                                                        c.data_ptr(), p.data_ptr(), M, N, K, ws, wsb, st),
                    "int8_gemm_partials")
     return c, p
 
@@ -105,7 +143,7 @@ def int8_index(q, w, k, k_s, causal=False, start=0, block_q=None, block_n=None, 
     _require_cuda(q, w, k, k_s)
     o = torch.empty(B, M, Nk, device=q.device, dtype=torch.float32)
     if B and M and Nk:
-        with torch.cuda.device(q.device):
+        with _OnDevice(q):
             _lib.check(_lib.load().dsv32_int8_index(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
                                                     o.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start),
                                                     _stream(q)), "int8_index")
@@ -132,7 +170,7 @@ def select_topk(scores: torch.Tensor, k: int, idx_offset: int = 0, cand_idx: tor
     else:
         cp, cld = None, 0
     if rows:
-        with torch.cuda.device(scores.device):
+        with _OnDevice(scores):
             _lib.check(_lib.load().dsv32_topk(scores.data_ptr(), rows, n, n, cp, cld, int(idx_offset), k,
                                               idx.data_ptr(), vals.data_ptr(), _stream(scores)), "select_topk")
     return idx, vals
@@ -152,7 +190,7 @@ def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_score
     vals = torch.empty(B, M, topk, device=q.device, dtype=torch.float32)
     if B and M:
         lib = _lib.load()
-        with torch.cuda.device(q.device):
+        with _OnDevice(q):
             s = _stream(q)
             _lib.check(lib.dsv32_int8_index(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
                                             scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start), s),

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define DSV32_ABI_VERSION 1
+#define DSV32_ABI_VERSION 2
 
 /* Status codes. */
 #define DSV32_OK 0
@@ -52,14 +52,25 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
  * kernels.py:71-101 (oracle reference.py:18-24).
  * a [m, k] int8, a_s [m, k/128] fp32, b [n, k] int8, b_s [n/128, k/128] fp32,
  * c [m, n] of c_dtype (DSV32_F32 / DSV32_BF16 / DSV32_F16). k % 128 == 0, n % 128 == 0, any m >= 1.
- * c[i, j] = sum_kb fp32(A_kb . B_kb) * (a_s[i, kb] * b_s[j / 128, kb]), accumulated in fp32. */
+ * c[i, j] = sum_kb fp32(A_kb . B_kb) * (a_s[i, kb] * b_s[j / 128, kb]), accumulated in fp32.
+ * workspace: device scratch of at least dsv32_int8_gemm_workspace_bytes(m, n, k) bytes, zero-filled
+ * before its first use; every completed launch leaves it reusable for any shape (after a launch that
+ * reported DSV32_ERR_DEVICE_TIMEOUT, zero it again). It lets the kernel balance K-blocks over all SMs
+ * (stream-K). NULL or too small: the kernel runs whole tiles per SM instead (same results up to fp32
+ * summation order). One workspace must not serve two launches that may run concurrently. */
 int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,
-                    int64_t m, int64_t n, int64_t k, void* stream);
+                    int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Debug form of dsv32_int8_gemm (same tensor-core path): also writes the exact int32 partial of
- * every 128-wide K block, partials [k/128, m, n] int32, and c [m, n] fp32. For parity tests. */
+/* Bytes of workspace dsv32_int8_gemm uses for (m, n, k) on the current device (0: none needed);
+ * a negative value is -status on error. */
+int64_t dsv32_int8_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
+/* Debug form of dsv32_int8_gemm (same tensor-core path and schedule): also writes the exact int32
+ * partial of every 128-wide K block, partials [k/128, m, n] int32, and c [m, n] fp32. For parity
+ * tests. */
 int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, float* c,
-                             int32_t* partials, int64_t m, int64_t n, int64_t k, void* stream);
+                             int32_t* partials, int64_t m, int64_t n, int64_t k, void* workspace,
+                             int64_t workspace_bytes, void* stream);
 
 /* int8_index: replaces kernels.py:165 int8_index(q, w, k, k_s, causal, start, ...) and its kernel
  * kernels.py:134-162 (oracle reference.py:27-34).

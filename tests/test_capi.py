@@ -38,7 +38,7 @@ def test_library_builds_and_exports_every_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.dsv32_abi_version() == 1
+    assert lib.dsv32_abi_version() == 2
     for code in range(6):
         assert lib.dsv32_status_string(code)
     assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")
@@ -49,21 +49,22 @@ def test_argument_validation_without_gpu():
     fake = ctypes.c_void_p(4096)  # never dereferenced: validation rejects before any launch
     # null pointers
     assert lib.dsv32_act_quant(None, 0, 4, 128, 0, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
-    assert lib.dsv32_int8_gemm(None, fake, fake, fake, fake, 0, 1, 128, 128, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_gemm(None, fake, fake, fake, fake, 0, 1, 128, 128, None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
     # the reference's shape asserts: N % 128, K % 128
     assert lib.dsv32_act_quant(fake, 0, 4, 100, 0, fake, fake, None) == _lib.DSV32_ERR_UNSUPPORTED
-    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 128, 100, None) == _lib.DSV32_ERR_UNSUPPORTED
-    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 100, 128, None) == _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 128, 100, None, 0, None) == _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 100, 128, None, 0, None) == _lib.DSV32_ERR_UNSUPPORTED
     # bad dtype code, bad head configuration, bad top-k
-    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 7, 4, 128, 128, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 7, 4, 128, 128, None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_int8_index(fake, fake, fake, fake, fake, 1, 4, 128, 48, 128, 0, 0, None) == \
         _lib.DSV32_ERR_UNSUPPORTED
     assert lib.dsv32_topk(fake, 4, 100, 100, None, 0, 0, 101, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_gemm_workspace_bytes(4, 100, 128) == -_lib.DSV32_ERR_UNSUPPORTED
     assert lib.dsv32_int8_index_topk(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 0, fake, fake,
                                      None) == _lib.DSV32_ERR_INVALID_ARG
     # misaligned operand
     odd = ctypes.c_void_p(4096 + 4)
-    assert lib.dsv32_int8_gemm(odd, fake, fake, fake, fake, 0, 4, 128, 128, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_gemm(odd, fake, fake, fake, fake, 0, 4, 128, 128, None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")

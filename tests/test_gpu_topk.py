@@ -92,3 +92,14 @@ def test_index_topk_decode():
     idx, vals = D.int8_index_topk(q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV), topk=2048, return_scores=False)
     ref = O.int8_index_ref(q.numpy(), w.numpy(), k.numpy(), ks.numpy())[0]
     assert O.topk_valid(npy(idx)[0], ref, 2048) or _near_tie_ok(npy(idx)[0], ref, 2048)
+
+
+def test_select_topk_with_infinities():
+    s = _scores(3, 5000, False, seed=9)
+    s[0, 10] = float("inf")
+    s[1, ::7] = float("-inf")
+    s[2, 100:4000] = float("-inf")  # 1100 values above -inf, k = 2048
+    idx, vals = D.select_topk(s.to(DEV), 2048)
+    ri, rv = O.topk_ref(s.numpy(), 2048)
+    np.testing.assert_array_equal(npy(idx), ri)
+    np.testing.assert_array_equal(npy(vals), rv)

@@ -31,6 +31,7 @@ SIGNATURES = {
     "dsv32_act_quant": (_i32, [_p, _i32, _i64, _i64, _i32, _p, _p, _p]),
     "dsv32_int8_gemm": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _p, _i64, _p]),
     "dsv32_int8_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "dsv32_int8_gemm_noalloc": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _p]),
     "dsv32_int8_gemm_partials": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "dsv32_int8_index": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _p]),
     "dsv32_topk": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p]),
@@ -73,7 +74,8 @@ class Dsv32Error(RuntimeError):
         lib = load()
         msg = lib.dsv32_status_string(status).decode()
         detail = lib.dsv32_last_error_message().decode()
-        super().__init__(f"{where}: {msg}" + (f" ({detail})" if detail and status == DSV32_ERR_CUDA else ""))
+        show = detail and status in (DSV32_ERR_CUDA, DSV32_ERR_UNSUPPORTED)
+        super().__init__(f"{where}: {msg}" + (f" ({detail})" if show else ""))
         self.status = status
 
 

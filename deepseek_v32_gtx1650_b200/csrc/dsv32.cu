@@ -41,7 +41,15 @@ struct DeviceInfo {
   bool sm100 = false;
   int num_sms = 0;
   int aq_blocks_per_sm[3] = {1, 1, 1};  // resident act_quant CTAs per SM, by input dtype
+  uint8_t* noalloc_scratch = nullptr;   // device address of g_noalloc_scratch on this device
 };
+
+// Scratch of dsv32_int8_gemm_noalloc: the stream-K counters and partial-tile slots of small-M
+// GEMMs, in a fixed array of the library's module instead of caller memory. Every GPU on which the
+// library's module is loaded holds these 10 MiB until the process exits; all calls share them.
+constexpr int64_t kNoAllocScratchBytes = int64_t(10) << 20;
+constexpr int64_t kNoAllocTilesCap = 1024;  // counter capacity inside the static scratch
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_mu;
 DeviceInfo g_dev[64];
@@ -133,6 +141,8 @@ struct GemmPlan {
   int64_t tiles, units;
   int grid;
   bool split;
+  int slot_rows;
+  int64_t ws_tiles_cap;
   int64_t ws_bytes;  // workspace the stream-K schedule needs (0 when data-parallel)
 };
 
@@ -140,16 +150,18 @@ struct GemmPlan {
 // fewer tiles than SMs (decode-sized m): there it is the only way to use every SM. With at least a
 // wave of tiles, whole tiles per SM measured faster on B200 than splitting tiles (the partial-tile
 // round trip through the workspace costs more than the tail wave it removes).
-GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k, int num_sms) {
+GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k, int num_sms,
+                   int64_t ws_tiles_cap = dsv32::gemm::kMaxSplitTiles, int slot_rows = dsv32::gemm::kBM) {
   GemmPlan p;
   p.BN = (n % 256 == 0) ? 256 : 128;
   p.tiles = ((m + 127) / 128) * ((n + p.BN - 1) / p.BN);
   p.units = p.tiles * (k / 128);
-  p.split = p.tiles < num_sms && p.tiles <= dsv32::gemm::kMaxSplitTiles;
+  p.split = p.tiles < num_sms && p.tiles <= ws_tiles_cap;
+  p.slot_rows = slot_rows;
+  p.ws_tiles_cap = ws_tiles_cap;
   if (p.split) {
     p.grid = static_cast<int>(p.units < num_sms ? p.units : num_sms);
-    p.ws_bytes = (p.BN == 256) ? dsv32::gemm::workspace_bytes<256>(p.grid)
-                               : dsv32::gemm::workspace_bytes<128>(p.grid);
+    p.ws_bytes = dsv32::gemm::workspace_bytes(p.BN, p.grid, ws_tiles_cap, p.slot_rows);
   } else {
     p.grid = static_cast<int>(p.tiles < num_sms ? p.tiles : num_sms);
     p.ws_bytes = 0;
@@ -168,6 +180,41 @@ int gemm_check(const int8_t* a, const float* a_s, const int8_t* b, const float* 
   return DSV32_OK;
 }
 
+// Encodes the operand tensor maps and launches the kernel for a plan (ws: NULL = data-parallel).
+int gemm_launch(const GemmPlan& plan, const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c,
+                int c_dtype, int64_t m, int64_t n, int64_t k, int32_t* partials, uint8_t* ws, void* stream) {
+  CUtensorMap tmA, tmB;
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(k)};
+  const uint32_t boxA[2] = {128, 128};
+  const uint32_t boxB[2] = {128, static_cast<uint32_t>(plan.BN)};
+  if (int st = encode_i8_map(&tmA, a, 2, dimsA, strides, boxA)) return st;
+  if (int st = encode_i8_map(&tmB, b, 2, dimsB, strides, boxB)) return st;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace dsv32::gemm;
+  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  const uint32_t ok = partials ? kOutF32 : static_cast<uint32_t>(c_dtype);
+  const int cap = static_cast<int>(plan.ws_tiles_cap), sr = plan.slot_rows;
+  if (plan.BN == 256) {
+    if (partials)
+      int8_gemm_kernel<256, true><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                 ki, partials, ws, cap, sr);
+    else
+      int8_gemm_kernel<256, false><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                  ki, nullptr, ws, cap, sr);
+  } else {
+    if (partials)
+      int8_gemm_kernel<128, true><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                 ki, partials, ws, cap, sr);
+    else
+      int8_gemm_kernel<128, false><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
+                                                                                  ki, nullptr, ws, cap, sr);
+  }
+  return launch_check("int8_gemm_kernel launch");
+}
+
 int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype, int64_t m,
               int64_t n, int64_t k, int32_t* partials, void* workspace, int64_t workspace_bytes, void* stream) {
   if (int st = gemm_check(a, a_s, b, b_s, c, c_dtype, m, n, k)) return st;
@@ -184,35 +231,7 @@ int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b
   }
   uint8_t* ws = plan.split ? static_cast<uint8_t*>(workspace) : nullptr;
 
-  CUtensorMap tmA, tmB;
-  const uint64_t dimsA[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
-  const uint64_t dimsB[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
-  const uint64_t strides[1] = {static_cast<uint64_t>(k)};
-  const uint32_t boxA[2] = {128, 128};
-  const uint32_t boxB[2] = {128, static_cast<uint32_t>(plan.BN)};
-  if (int st = encode_i8_map(&tmA, a, 2, dimsA, strides, boxA)) return st;
-  if (int st = encode_i8_map(&tmB, b, 2, dimsB, strides, boxB)) return st;
-
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  using namespace dsv32::gemm;
-  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
-  const uint32_t ok = partials ? kOutF32 : static_cast<uint32_t>(c_dtype);
-  if (plan.BN == 256) {
-    if (partials)
-      int8_gemm_kernel<256, true><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                 ki, partials, ws);
-    else
-      int8_gemm_kernel<256, false><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                  ki, nullptr, ws);
-  } else {
-    if (partials)
-      int8_gemm_kernel<128, true><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                 ki, partials, ws);
-    else
-      int8_gemm_kernel<128, false><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                  ki, nullptr, ws);
-  }
-  return launch_check("int8_gemm_kernel launch");
+  return gemm_launch(plan, a, a_s, b, b_s, c, c_dtype, m, n, k, partials, ws, stream);
 }
 
 template <int H, int D>
@@ -365,6 +384,38 @@ int64_t dsv32_int8_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   DeviceInfo* info = nullptr;
   if (int st = device_setup(&dev, &info)) return -st;
   return gemm_plan(m, n, k, info->num_sms).ws_bytes;
+}
+
+int dsv32_int8_gemm_noalloc(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c,
+                            int c_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
+  if (int st = gemm_check(a, a_s, b, b_s, c, c_dtype, m, n, k)) return st;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+  GemmPlan plan = gemm_plan(m, n, k, info->num_sms, kNoAllocTilesCap, dsv32::gemm::slot_rows_for(m));
+  uint8_t* ws = nullptr;
+  if (plan.split) {
+    if (plan.ws_bytes > kNoAllocScratchBytes) {
+      t_last_error = "dsv32_int8_gemm_noalloc: this problem needs " + std::to_string(plan.ws_bytes) +
+                     " bytes of scratch, the static scratch holds " + std::to_string(kNoAllocScratchBytes) +
+                     " (problems with fewer 128-row tiles than SMs fit up to m = 32); use dsv32_int8_gemm";
+      return DSV32_ERR_UNSUPPORTED;
+    }
+    {
+      // First call on this device (with it current): look up the array's device address once.
+      std::lock_guard<std::mutex> lock(g_mu);
+      if (!info->noalloc_scratch) {
+        void* ptr = nullptr;
+        DSV32_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+        info->noalloc_scratch = static_cast<uint8_t*>(ptr);
+      }
+      ws = info->noalloc_scratch;
+    }
+    // The tile counters must start at zero; the slots need no clearing.
+    DSV32_CUDA_TRY(cudaMemsetAsync(ws, 0, dsv32::gemm::counter_bytes(kNoAllocTilesCap),
+                                   static_cast<cudaStream_t>(stream)));
+  }
+  return gemm_launch(plan, a, a_s, b, b_s, c, c_dtype, m, n, k, nullptr, ws, stream);
 }
 
 int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, float* c,

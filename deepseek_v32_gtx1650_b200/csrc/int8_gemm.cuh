@@ -61,20 +61,22 @@ struct Smem {
   static constexpr int kOffAbort = kOffTmem + 4;
   static constexpr int kBytes = kOffAbort + 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment (SWIZZLE_128B)
-  static constexpr int64_t kSlotFloats = int64_t(kBM) * BN;  // one partial tile, fp32
 };
 
 enum : uint32_t { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
 
-// Workspace layout (bytes): [counters: kMaxSplitTiles x 8 epilogue warps int32 (fixed size, so
-// the counters never share bytes with slot data whatever the problem shape)]
-// [2 * grid slots of kBM x BN fp32]. Slot 2c holds CTA c's first segment, slot 2c+1 its last one.
+// Workspace layout (bytes): [counters: tiles_cap x 8 epilogue warps int32; a fixed capacity per
+// workspace, so the counters never share bytes with slot data whatever the problem shape]
+// [2 * grid slots of slot_rows x BN fp32, column-major]. Slot 2c holds CTA c's first segment, slot
+// 2c+1 its last one; slot_rows = min(128, M rounded up to 32) (rows past M are never written).
 // The counters must be zero before the first launch; every completed launch leaves them zero.
-constexpr int64_t kMaxSplitTiles = 65536;
-__host__ __device__ constexpr int64_t counter_bytes() { return kMaxSplitTiles * kEpiWarps * 4; }
-template <int BN>
-__host__ __device__ inline int64_t workspace_bytes(int grid) {
-  return counter_bytes() + int64_t(2) * grid * Smem<BN>::kSlotFloats * 4;
+constexpr int64_t kMaxSplitTiles = 65536;  // counter capacity of caller-provided workspaces
+__host__ __device__ constexpr int64_t counter_bytes(int64_t tiles_cap) { return tiles_cap * kEpiWarps * 4; }
+__host__ __device__ inline int slot_rows_for(int64_t m) {
+  return static_cast<int>(m >= kBM ? kBM : ((m + 31) / 32) * 32);
+}
+__host__ __device__ inline int64_t workspace_bytes(int BN, int grid, int64_t tiles_cap, int slot_rows) {
+  return counter_bytes(tiles_cap) + int64_t(2) * grid * slot_rows * BN * 4;
 }
 
 struct Sched {
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ a_s, const float* __restrict__ b_s, void* __restrict__ C,
                      uint32_t out_kind, int M, int N, int K, int32_t* __restrict__ partials,
-                     uint8_t* __restrict__ workspace) {
+                     uint8_t* __restrict__ workspace, int ws_tiles_cap, int slot_rows) {
   using L = Smem<BN>;
   constexpr int kCols = BN / 2;  // columns per epilogue thread
   extern __shared__ uint8_t smem_raw[];
@@ -328,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r_local = wq * 32 + lane;  // row within the tile
     const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wh * kCols);
     int* counters = reinterpret_cast<int*>(workspace);
-    float* slots = workspace ? reinterpret_cast<float*>(workspace + counter_bytes()) : nullptr;
+    float* slots = workspace ? reinterpret_cast<float*>(workspace + counter_bytes(ws_tiles_cap)) : nullptr;
+    const int64_t slot_floats = static_cast<int64_t>(slot_rows) * BN;
     bool ok = true;
     // Arm both accumulators with the conversion bias.
 #pragma unroll
@@ -413,12 +416,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this sub-tile last (one counter per tile and warp) reduces and stores. Warp-local: no
       // barrier across warps, so an aborting warp can never strand the others.
       const int slot = 2 * blockIdx.x + (first_seg ? 0 : 1);
-      float* my_slot = slots + slot * L::kSlotFloats + static_cast<int64_t>(wh) * kCols * kBM;
+      float* my_slot = slots + slot * slot_floats + static_cast<int64_t>(wh) * kCols * slot_rows;
       if (row_ok && cols_ok) {
 #pragma unroll
         for (int j = 0; j < kCols / 2; ++j) {  // column-major slot: lanes write consecutive rows
-          __stcg(my_slot + (2 * j) * kBM + r_local, acc[j].x);
-          __stcg(my_slot + (2 * j + 1) * kBM + r_local, acc[j].y);
+          __stcg(my_slot + (2 * j) * slot_rows + r_local, acc[j].x);
+          __stcg(my_slot + (2 * j + 1) * slot_rows + r_local, acc[j].y);
         }
       }
       __threadfence();
@@ -444,10 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int cc = c_first; cc <= c_last; ++cc) {
         const int first_tile_of_cc = static_cast<int>(sch.ubeg(cc) / sch.KG);
         const int s = 2 * cc + (first_tile_of_cc == tile ? 0 : 1);
-        const float* ps = slots + s * L::kSlotFloats + static_cast<int64_t>(wh) * kCols * kBM;
+        const float* ps = slots + s * slot_floats + static_cast<int64_t>(wh) * kCols * slot_rows;
 #pragma unroll
         for (int j = 0; j < kCols / 2; ++j) {
-          const float2 v = make_float2(__ldcg(ps + (2 * j) * kBM + r_local), __ldcg(ps + (2 * j + 1) * kBM + r_local));
+          const float2 v = make_float2(__ldcg(ps + (2 * j) * slot_rows + r_local),
+                                       __ldcg(ps + (2 * j + 1) * slot_rows + r_local));
           acc[j] = __fadd2_rn(acc[j], v);
         }
       }

@@ -72,6 +72,23 @@ int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b,
                              int32_t* partials, int64_t m, int64_t n, int64_t k, void* workspace,
                              int64_t workspace_bytes, void* stream);
 
+/* int8_gemm for callers that cannot allocate device memory. No counterpart in the reference.
+ * Some hosts own every byte of device memory (an inference engine that plans all buffers into its
+ * own arena and forbids plugins from calling cudaMalloc, or a process running under a fixed memory
+ * budget), so they cannot hand dsv32_int8_gemm a workspace. This variant takes the same inputs and
+ * output and allocates nothing: its scratch is a 10 MiB array inside the library, present on every
+ * GPU that loads the library until the process exits. It computes what dsv32_int8_gemm computes.
+ *  - The first call on a device (with that device current) looks up the array's address.
+ *  - Each call clears the array's tile counters on `stream` before the kernel.
+ *  - All calls share the one array: calls that may overlap on the GPU (other streams, other host
+ *    threads) race and must be serialised by the caller.
+ *  - Problems with at least one wave of 128-row tiles (one per SM) need no scratch and run at any
+ *    size. Smaller problems spread their K blocks over all SMs through the scratch; those that
+ *    would need more than 10 MiB (for example m = 64 with n = 7168) return DSV32_ERR_UNSUPPORTED,
+ *    with the needed size in dsv32_last_error_message(). */
+int dsv32_int8_gemm_noalloc(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c,
+                            int c_dtype, int64_t m, int64_t n, int64_t k, void* stream);
+
 /* int8_index: replaces kernels.py:165 int8_index(q, w, k, k_s, causal, start, ...) and its kernel
  * kernels.py:134-162 (oracle reference.py:27-34).
  * q [batch, m, heads, dim] int8, w [batch, m, heads] fp32, k [batch, n, dim] int8, k_s [batch, n] fp32,

@@ -1,0 +1,59 @@
+"""dsv32_int8_gemm_noalloc: the GEMM entry point for callers that cannot allocate device memory
+(hosts that plan every device buffer themselves and forbid plugins from calling cudaMalloc).
+
+It must give what the regular entry point gives, call after call, using only the scratch array
+built into the library. This file is collected last so that a failure here leaves every other test
+already run; it passes alone in a fresh process and after the rest of the suite.
+"""
+import numpy as np
+import pytest
+import torch
+
+import deepseek_v32_gtx1650_b200 as D
+from deepseek_v32_gtx1650_b200 import _lib, workloads
+from tests.gpu_util import DEV, assert_no_device_error, npy, rel_err
+
+pytestmark = pytest.mark.gpu
+
+_CODE = {torch.float32: _lib.DSV32_F32, torch.bfloat16: _lib.DSV32_BF16, torch.float16: _lib.DSV32_F16}
+
+
+def _noalloc(a, a_s, b, b_s, c):
+    lib = _lib.load()
+    M, K = a.shape
+    N = b.shape[0]
+    return lib.dsv32_int8_gemm_noalloc(a.data_ptr(), a_s.data_ptr(), b.data_ptr(), b_s.data_ptr(), c.data_ptr(),
+                                       _CODE[c.dtype], M, N, K, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("M,N,K,dt", [(32, 7168, 2048, torch.float32), (1, 2048, 7168, torch.float32),
+                                      (20, 640, 512, torch.float32), (32, 7168, 2048, torch.bfloat16),
+                                      (4096, 2048, 7168, torch.float32)])
+def test_noalloc_matches_regular_entry_point_on_two_calls(M, N, K, dt):
+    a, a_s, b, b_s = (t.to(DEV) for t in workloads.gemm_inputs_uniform(M, N, K, seed=M + N))
+    ref = D.int8_gemm(a, a_s, b, b_s, out_dtype=dt)  # regular entry point, caller-provided workspace
+    outs = [torch.full((M, N), float("nan"), device=DEV, dtype=dt) for _ in range(2)]
+    torch.cuda.synchronize()
+    free = []
+    for c in outs:  # two calls in a row into fresh outputs
+        _lib.check(_noalloc(a, a_s, b, b_s, c), "dsv32_int8_gemm_noalloc")
+        torch.cuda.synchronize()
+        free.append(torch.cuda.mem_get_info()[0])
+    assert free[0] == free[1], "device memory changed between calls"
+    tol = 1e-5 if dt == torch.float32 else 1e-2
+    for c in outs:
+        assert rel_err(npy(c.float()), npy(ref.float()).astype(np.float64)) < tol
+    assert torch.equal(outs[0], outs[1])
+    assert_no_device_error()
+
+
+def test_noalloc_rejects_problems_beyond_its_scratch():
+    """m = 64 over n = 7168 has fewer tiles than SMs and needs about 19 MiB of scratch."""
+    M, N, K = 64, 7168, 2048
+    a, a_s, b, b_s = (t.to(DEV) for t in workloads.gemm_inputs_uniform(M, N, K, seed=1))
+    c = torch.zeros(M, N, device=DEV)
+    st = _noalloc(a, a_s, b, b_s, c)
+    assert st == _lib.DSV32_ERR_UNSUPPORTED
+    assert "static scratch" in _lib.load().dsv32_last_error_message().decode()
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(c) == 0  # nothing was launched

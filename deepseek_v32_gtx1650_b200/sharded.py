@@ -45,10 +45,10 @@ def gather_candidates(idx: torch.Tensor, vals: torch.Tensor, group=None):
     One collective: ids and value bits travel together as int32."""
     world = dist.get_world_size(group)
     rows, k = idx.shape
-    packed = torch.stack([idx, vals.view(torch.int32)]).contiguous()  # [2, rows, k]
-    out = torch.empty((world,) + tuple(packed.shape), dtype=torch.int32, device=packed.device)
-    dist.all_gather_into_tensor(out, packed, group=group)
-    cand = out.permute(1, 2, 0, 3).reshape(2, rows, world * k)  # row-major: rank 0's k, rank 1's k, ...
+    packed = torch.stack([idx, vals.view(torch.int32)]).contiguous().view(-1)  # [2 * rows * k]
+    out = torch.empty(world * packed.numel(), dtype=torch.int32, device=packed.device)
+    dist.all_gather_into_tensor(out, packed, group=group)  # concatenated form: NCCL and gloo
+    cand = out.view(world, 2, rows, k).permute(1, 2, 0, 3).reshape(2, rows, world * k)  # rank 0's k, rank 1's k..
     return cand[0].contiguous(), cand[1].contiguous().view(torch.float32)
 
 
@@ -76,6 +76,6 @@ def gather_columns(c_local: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather equal-width column slices [M, n_r] into the full [M, world * n_r] output."""
     world = dist.get_world_size(group)
     M, nr = c_local.shape
-    out = torch.empty(world, M, nr, dtype=c_local.dtype, device=c_local.device)
+    out = torch.empty(world * M, nr, dtype=c_local.dtype, device=c_local.device)
     dist.all_gather_into_tensor(out, c_local.contiguous(), group=group)
-    return out.permute(1, 0, 2).reshape(M, world * nr)
+    return out.view(world, M, nr).permute(1, 0, 2).reshape(M, world * nr)

@@ -238,25 +238,8 @@ DSV32_DEV void tmem_wait_ld16(uint32_t (&r)[16]) {
                : "memory");
 }
 
-DSV32_DEV void tmem_fill16(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
 
-// Fill 32 lanes x 32 columns of TMEM with one 32-bit value (no wait).
-DSV32_DEV void tmem_fill32(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
 
-DSV32_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Register re-balancing between warpgroups (all 4 warps of a warpgroup execute it).
 template <uint32_t N>
@@ -268,9 +251,3 @@ DSV32_DEV void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :
 DSV32_DEV void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-
-// int32 accumulators are pre-biased with these bits: bits(1.5 * 2^23). For |x| < 2^22,
-// the bits (BIAS + x) read as a float equal 1.5 * 2^23 + x exactly, so one exact FADD of
-// -1.5 * 2^23 converts the tensor-core integer to fp32 (no I2F on the conversion pipe).
-constexpr uint32_t kI32FloatBiasBits = 0x4B400000u;
-constexpr float kI32FloatBias = 12582912.0f;

@@ -17,9 +17,9 @@
 // Key tiles past the causal limit of every query in the block are not loaded or multiplied:
 // the epilogue writes -inf for them directly (the reference's tile skip, kernels.py:145-148).
 //
-// relu and the int32 -> fp32 conversion use the same pre-biased accumulator as int8_gemm:
-// bits = bits(1.5*2^23) + logit, so relu is an integer max against the bias bits and the
-// conversion is one exact FADD. |logit| <= D*127*127 < 2^21.
+// Per logit: relu as an integer max with 0, an exact int32 -> fp32 conversion
+// (|logit| <= D*127*127 < 2^24) and one fused multiply-add with the head weight (packed f32x2).
+// The first MMA of each key tile overwrites the accumulator, so buffers need no clearing.
 #pragma once
 #include "common.cuh"
 
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * kNmma;
 #pragma unroll
         for (int k = 0; k < D / 32; ++k) {
-          umma_i8(d_tmem, make_sdesc(k_addr + 32 * k, D), make_sdesc(sQ + 32 * k, D), idesc, 1u);
+          umma_i8(d_tmem, make_sdesc(k_addr + 32 * k, D), make_sdesc(sQ + 32 * k, D), idesc, k > 0 ? 1u : 0u);
         }
         umma_commit(kempty_bar(stage));
         umma_commit(tfull_bar(buf));
@@ -225,19 +225,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (n_mma_tiles > 0) {
       const float4* w_half = reinterpret_cast<const float4*>(sW + wh * C::kColsPerHalf);
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-#pragma unroll
-        for (int c = 0; c < C::kColsPerHalf / 32; ++c) tmem_fill32(t_lane + b * kNmma + c * 32, kI32FloatBiasBits);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
+      __syncwarp();  // both accumulators start free
       if (lane == 0) {
         mbar_arrive(tempty_bar(0));
         mbar_arrive(tempty_bar(1));
       }
-      const float2 nbias = make_float2(-kI32FloatBias, -kI32FloatBias);
       for (int i = 0; i < n_mma_tiles; ++i) {
         const uint32_t buf = uint32_t(i) & 1u;
         const int n = (un.kt0 + i) * kKeysPerTile + wq * 32 + lane;
@@ -260,7 +252,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t(&r)[32] = (c & 1) ? rb : ra;
           uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
           if (c + 1 < C::kColsPerHalf / 32) tmem_ld32_async(tb + (c + 1) * 32, nxt);
-          tmem_fill32(tb + c * 32, kI32FloatBiasBits);  // re-arm the finished chunk
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
             const float4 w4 = w_half[c * 8 + j4];  // same address across the warp: broadcast
@@ -268,17 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int j = 4 * j4 + 2 * h;
-              const int r0 = max(static_cast<int>(r[j]), static_cast<int>(kI32FloatBiasBits));
-              const int r1 = max(static_cast<int>(r[j + 1]), static_cast<int>(kI32FloatBiasBits));
-              float2 v = make_float2(__int_as_float(r0), __int_as_float(r1));
-              v = __fadd2_rn(v, nbias);  // exact relu(logit) in fp32
+              const float2 v = make_float2(static_cast<float>(max(static_cast<int>(r[j]), 0)),
+                                           static_cast<float>(max(static_cast<int>(r[j + 1]), 0)));  // relu
               const float2 wv = h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
               acc[q] = __ffma2_rn(v, wv, acc[q]);
             }
           }
           if (c + 1 < C::kColsPerHalf / 32) tmem_wait_ld32(nxt);
         }
-        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty_bar(buf));

@@ -238,8 +238,17 @@ DSV32_DEV void tmem_wait_ld16(uint32_t (&r)[16]) {
                : "memory");
 }
 
-
-
+// relu(x) * 2^-22 for an int32 x with |x| < 2^22, exactly, on the FP32 pipe (no integer op).
+// The bit pattern of x >= 0 read as fp32 is the subnormal x * 2^-149; multiplied by 2^127 it is
+// x * 2^-22, exact because x has at most 22 significant bits. For -2^22 < x < 0 the pattern is a
+// NaN (exponent field all ones), and a saturating multiply returns +0 for a NaN result. The
+// saturation bound 1.0 is never reached since x * 2^-22 < 1. Subnormal inputs are kept
+// (no .ftz), which the FP32 pipe handles at full rate.
+DSV32_DEV float relu_i32_x2m22(uint32_t bits) {
+  float r;
+  asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(r) : "f"(__uint_as_float(bits)), "f"(0x1p127f));
+  return r;
+}
 
 // Register re-balancing between warpgroups (all 4 warps of a warpgroup execute it).
 template <uint32_t N>

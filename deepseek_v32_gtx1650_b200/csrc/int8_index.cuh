@@ -17,8 +17,11 @@
 // Key tiles past the causal limit of every query in the block are not loaded or multiplied:
 // the epilogue writes -inf for them directly (the reference's tile skip, kernels.py:145-148).
 //
-// Per logit: relu as an integer max with 0, an exact int32 -> fp32 conversion
-// (|logit| <= D*127*127 < 2^24) and one fused multiply-add with the head weight (packed f32x2).
+// Per logit: relu and the int32 -> fp32 conversion in one saturating fp32 multiply of the raw bits
+// (relu_i32_x2m22, exact for |logit| <= D*128*128 <= 2^21, giving relu * 2^-22), then one fused
+// multiply-add with the head weight (packed f32x2); the 2^-22 is folded into k_s. Everything runs on
+// the FP32 pipe; the results equal relu-then-convert bit for bit (power-of-two scalings, no
+// subnormal intermediates for any realistic head weight).
 // The first MMA of each key tile overwrites the accumulator, so buffers need no clearing.
 #pragma once
 #include "common.cuh"
@@ -233,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < n_mma_tiles; ++i) {
         const uint32_t buf = uint32_t(i) & 1u;
         const int n = (un.kt0 + i) * kKeysPerTile + wq * 32 + lane;
-        const float ks = (n < N) ? __ldg(k_s + static_cast<int64_t>(un.b) * N + n) : 0.f;
+        // k_s * 2^22 undoes the 2^-22 of the relu step (power-of-two scalings: same rounding).
+        const float ks = (n < N) ? __ldg(k_s + static_cast<int64_t>(un.b) * N + n) * 0x1p22f : 0.f;
         if (!mbar_wait_warp(tfull_bar(buf), (uint32_t(i) >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
           ok = false;
           break;
@@ -259,8 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int j = 4 * j4 + 2 * h;
-              const float2 v = make_float2(static_cast<float>(max(static_cast<int>(r[j]), 0)),
-                                           static_cast<float>(max(static_cast<int>(r[j + 1]), 0)));  // relu
+              const float2 v = make_float2(relu_i32_x2m22(r[j]), relu_i32_x2m22(r[j + 1]));
               const float2 wv = h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
               acc[q] = __ffma2_rn(v, wv, acc[q]);
             }

@@ -250,9 +250,10 @@ int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w,
   chunks = (nt + tpc - 1) / tpc;
   const int64_t units = batch * nqb * chunks;
   if (units > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
-  int8_index_kernel<H, D><<<static_cast<unsigned>(units), kThreads, C::kAlloc, st>>>(
+  const int64_t grid = units < num_sms ? units : num_sms;  // persistent: one CTA per SM
+  int8_index_kernel<H, D><<<static_cast<unsigned>(grid), kThreads, C::kAlloc, st>>>(
       tmQ, tmK, w, k_s, out, static_cast<int>(m), static_cast<int>(n), causal, static_cast<long long>(start),
-      static_cast<int>(tpc), static_cast<int>(chunks));
+      static_cast<int>(tpc), static_cast<int>(chunks), static_cast<int>(units));
   return launch_check("int8_index_kernel launch");
 }
 

@@ -7,15 +7,20 @@
 // reference layout: q [B, M, H, D] int8, k [B, N, D] int8, w [B, M, H] fp32, k_s [B, N] fp32,
 // out [B, M, N] fp32.
 //
-// Mapping (one CTA per work unit = (batch, block of QB queries, chunk of 128-key tiles)):
-//   UMMA M = 128 keys (TMEM lanes), UMMA N = QB*H (query, head) pairs (QB*H = 256), K = D.
-//   Each epilogue thread owns one key and reduces relu(logit) * w over the heads of its
-//   queries entirely in registers (no cross-lane reduction), then scales by k_s and stores.
-//   warp 8 = TMA producer (Q block once, then a 4-stage ring of key tiles),
-//   warp 9 = MMA issuer (double-buffered int32 TMEM accumulator), warps 0-7 = epilogue;
-//   warp w reads TMEM lanes 32*(w%4).. and the query half w/4 of the columns.
-// Key tiles past the causal limit of every query in the block are not loaded or multiplied:
-// the epilogue writes -inf for them directly (the reference's tile skip, kernels.py:145-148).
+// Mapping: UMMA M = 128 keys (TMEM lanes), UMMA N = QB*H (query, head) pairs (QB*H = 256), K = D.
+// A work unit is (batch, block of QB queries, chunk of 128-key tiles). The kernel is persistent:
+// one CTA per SM walks its units (heaviest causal query blocks first, dealt out in snake order so
+// every SM gets about the same number of tiles) and keeps its TMEM, barriers and pipelines across
+// units, so consecutive units overlap (the next unit's Q and key tiles load while the current
+// one is still in the epilogue).
+//   warp 8      TMA producer: the unit's Q block into one of two Q buffers, then its key tiles
+//               into a 4-stage ring.
+//   warp 9      MMA issuer: D / 32 MMAs per key tile into one of two int32 TMEM accumulators.
+//   warps 0-7   epilogue: each thread owns one key and reduces relu(logit) * w over the heads of
+//               its queries entirely in registers (no cross-lane reduction), then scales by k_s and
+//               stores. Warp w reads TMEM lanes 32*(w%4).. and the query half w/4 of the columns.
+//   warps 10-11 write -inf for the key tiles that no query of a unit can see (causal), which are
+//               neither loaded nor multiplied (the reference's tile skip, kernels.py:145-148).
 //
 // Per logit: relu and the int32 -> fp32 conversion in one saturating fp32 multiply of the raw bits
 // (relu_i32_x2m22, exact for |logit| <= D*128*128 <= 2^21, giving relu * 2^-22), then one fused
@@ -32,7 +37,7 @@ namespace index {
 constexpr int kKeysPerTile = 128;
 constexpr int kStages = 4;
 constexpr int kEpiWarps = 8;
-constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 idle
+constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 -inf writers
 // Launch: 384 threads x 168 registers = 64512. setmaxnreg moves them to the epilogue:
 // 2 warpgroups x 128 x 200 + 1 warpgroup x 128 x 104 = 64512 (and per sub-partition
 // 200 + 200 + 104 = 504 <= 512).
@@ -40,6 +45,7 @@ constexpr uint32_t kEpiRegs = 200;
 constexpr uint32_t kCtlRegs = 104;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
+constexpr int kFillWarp0 = kEpiWarps + 2;
 constexpr int kNmma = 256;  // QB * H
 
 template <int H, int D>
@@ -47,12 +53,14 @@ struct Cfg {
   static constexpr int QB = kNmma / H;                 // queries per block
   static constexpr int kQBytes = QB * H * D;           // Q tile bytes
   static constexpr int kKBytes = kKeysPerTile * D;     // key tile bytes per stage
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
-  static constexpr int kOffW = kOffK + kStages * kKBytes;
-  static constexpr int kOffBar = kOffW + QB * H * 4;
-  // qfull, kfull[kStages], kempty[kStages], tfull[2], tempty[2], mma_done
-  static constexpr int kNumBars = 2 + 2 * kStages + 4;
+  static constexpr int kColsPerHalf = kNmma / 2;       // columns per epilogue warpgroup
+  static constexpr int kQPerHalf = QB / 2;
+  static constexpr int kOffQ = 0;                      // two Q buffers
+  static constexpr int kOffK = kOffQ + 2 * kQBytes;
+  static constexpr int kOffW = kOffK + kStages * kKBytes;  // per epilogue warp: its half's weights
+  static constexpr int kOffBar = kOffW + kEpiWarps * kColsPerHalf * 4;
+  // qfull[2], qempty[2], kfull[kStages], kempty[kStages], tfull[2], tempty[2], mma_done
+  static constexpr int kNumBars = 9 + 2 * kStages;
   static constexpr int kOffTmem = kOffBar + 8 * kNumBars;
   static constexpr int kOffAbort = kOffTmem + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -60,8 +68,6 @@ struct Cfg {
   static_assert(QB * H == kNmma, "QB*H must be 256");
   static_assert(D == 64 || D == 128, "head dim must be 64 or 128");
   static_assert(QB % 2 == 0, "two query halves");
-  static constexpr int kColsPerHalf = kNmma / 2;       // columns per epilogue warpgroup
-  static constexpr int kQPerHalf = QB / 2;
 };
 
 DSV32_DEV void drain_wait(uint32_t bar, uint32_t parity) {
@@ -75,12 +81,11 @@ struct Unit {
   int b, m0, kt0, kt_vis, kt1;
 };
 
-// Work unit of this CTA. Units are ordered so the heaviest causal query blocks start first.
-DSV32_DEV Unit decode_unit(int M, int N, int QB, int causal, long long start, int tiles_per_chunk,
+// Work unit number `idx`. Units are numbered so that the heaviest causal query blocks come first.
+DSV32_DEV Unit decode_unit(int idx, int M, int N, int QB, int causal, long long start, int tiles_per_chunk,
                            int num_chunks) {
   const int NQB = (M + QB - 1) / QB;
   const int NT = (N + kKeysPerTile - 1) / kKeysPerTile;
-  const int idx = blockIdx.x;
   const int c = idx % num_chunks;
   const int rest = idx / num_chunks;
   int qb = rest % NQB;
@@ -94,17 +99,26 @@ DSV32_DEV Unit decode_unit(int M, int N, int QB, int causal, long long start, in
   if (causal) {
     const long long m_last = min(M - 1, u.m0 + QB - 1);
     const long long lim = start + m_last + 1;  // keys [0, lim) are visible to some query
-    const long long vis_tiles = (lim + kKeysPerTile - 1) / kKeysPerTile;
+    const long long vis_tiles = lim <= 0 ? 0 : (lim + kKeysPerTile - 1) / kKeysPerTile;
     u.kt_vis = static_cast<int>(max(static_cast<long long>(u.kt0), min(static_cast<long long>(u.kt1), vis_tiles)));
   }
   return u;
+}
+
+// The r-th unit of this CTA in snake order (round r covers units [r*G, (r+1)*G); odd rounds run
+// backwards), or -1 past the end.
+DSV32_DEV int unit_of_round(int r, int units) {
+  const int G = static_cast<int>(gridDim.x);
+  const long long idx = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - static_cast<int>(blockIdx.x))
+                                                                 : static_cast<int>(blockIdx.x));
+  return idx < units ? static_cast<int>(idx) : -1;
 }
 
 template <int H, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_index_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const float* __restrict__ w, const float* __restrict__ k_s, float* __restrict__ out, int M,
-                      int N, int causal, long long start, int tiles_per_chunk, int num_chunks) {
+                      int N, int causal, long long start, int tiles_per_chunk, int num_chunks, int units) {
   using C = Cfg<H, D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -113,31 +127,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const uint32_t sQ = base + C::kOffQ;
   const uint32_t sK = base + C::kOffK;
-  float* sW = reinterpret_cast<float*>(smem + C::kOffW);
   const uint32_t bar0 = base + C::kOffBar;
-  const uint32_t qfull_bar = bar0;
-  auto kfull_bar = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto kempty_bar = [&](int s) { return bar0 + 8u * (1 + kStages + s); };
-  auto tfull_bar = [&](int b) { return bar0 + 8u * (1 + 2 * kStages + b); };
-  auto tempty_bar = [&](int b) { return bar0 + 8u * (3 + 2 * kStages + b); };
-  const uint32_t mma_done_bar = bar0 + 8u * (5 + 2 * kStages);
+  auto qfull_bar = [&](int b) { return bar0 + 8u * b; };
+  auto qempty_bar = [&](int b) { return bar0 + 8u * (2 + b); };
+  auto kfull_bar = [&](int s) { return bar0 + 8u * (4 + s); };
+  auto kempty_bar = [&](int s) { return bar0 + 8u * (4 + kStages + s); };
+  auto tfull_bar = [&](int b) { return bar0 + 8u * (4 + 2 * kStages + b); };
+  auto tempty_bar = [&](int b) { return bar0 + 8u * (6 + 2 * kStages + b); };
+  const uint32_t mma_done_bar = bar0 + 8u * (8 + 2 * kStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffAbort);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmem);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const Unit un = decode_unit(M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
-  const int n_mma_tiles = un.kt_vis - un.kt0;
 
   if (threadIdx.x == 0) {
-    mbar_init(qfull_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(qfull_bar(b), 1);
+      mbar_init(qempty_bar(b), 1);
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), kEpiWarps);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(kfull_bar(s), 1);
       mbar_init(kempty_bar(s), 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), kEpiWarps);
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
@@ -153,92 +166,152 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<kCtlRegs>();
   }
   if (warp == kProducerWarp) {
-    if (lane == 0 && n_mma_tiles > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
-      mbar_arrive_expect_tx(qfull_bar, C::kQBytes);
-      tma_load_3d(sQ, &tmQ, qfull_bar, 0, un.m0 * H, un.b);
       int stage = 0;
       uint32_t phase = 0;
-      int issued = 0;
-      for (int kt = un.kt0; kt < un.kt_vis; ++kt) {
-        if (!mbar_wait(kempty_bar(stage), phase ^ 1u, abort_flag, (KID_INDEX << 16) | 1)) break;
-        mbar_arrive_expect_tx(kfull_bar(stage), C::kKBytes);
-        tma_load_3d(sK + stage * C::kKBytes, &tmK, kfull_bar(stage), 0, kt * kKeysPerTile, un.b);
-        ++issued;
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+      int k_issued = 0, q_issued = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int idx = unit_of_round(r, units);
+        if (idx < 0) break;
+        const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
+        if (un.kt_vis == un.kt0) continue;  // nothing to multiply
+        const int qb = q_issued & 1;
+        if (!mbar_wait(qempty_bar(qb), ((q_issued >> 1) & 1) ^ 1u, abort_flag, (KID_INDEX << 16) | 6)) break;
+        mbar_arrive_expect_tx(qfull_bar(qb), C::kQBytes);
+        tma_load_3d(sQ + qb * C::kQBytes, &tmQ, qfull_bar(qb), 0, un.m0 * H, un.b);
+        ++q_issued;
+        for (int kt = un.kt0; kt < un.kt_vis; ++kt) {
+          if (!mbar_wait(kempty_bar(stage), phase ^ 1u, abort_flag, (KID_INDEX << 16) | 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(kfull_bar(stage), C::kKBytes);
+          tma_load_3d(sK + stage * C::kKBytes, &tmK, kfull_bar(stage), 0, kt * kKeysPerTile, un.b);
+          ++k_issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
-      for (int i = 0; i < kStages && i < issued; ++i) {
+      // Wait for the last loads issued into every buffer to land before the CTA can exit.
+      for (int i = 0; i < kStages && i < k_issued; ++i) {
         if (--stage < 0) {
           stage = kStages - 1;
           phase ^= 1u;
         }
         drain_wait(kfull_bar(stage), phase);
       }
-      drain_wait(qfull_bar, 0);
+      for (int j = max(0, q_issued - 2); j < q_issued; ++j) drain_wait(qfull_bar(j & 1), (j >> 1) & 1);
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0 && n_mma_tiles > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_i8(kKeysPerTile, kNmma);
-      bool ok = mbar_wait(qfull_bar, 0, abort_flag, (KID_INDEX << 16) | 2);
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; ok && i < n_mma_tiles; ++i) {
-        const uint32_t buf = uint32_t(i) & 1u;
-        if (!mbar_wait(tempty_bar(buf), (uint32_t(i) >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 3) ||
-            !mbar_wait(kfull_bar(stage), phase, abort_flag, (KID_INDEX << 16) | 4))
-          break;
-        tc_fence_after();
-        const uint32_t k_addr = sK + stage * C::kKBytes;
-        const uint32_t d_tmem = tmem_base + buf * kNmma;
+      uint32_t i = 0;  // key tiles multiplied by this CTA (selects the TMEM buffer)
+      int j = 0;       // units multiplied by this CTA (selects the Q buffer)
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int idx = unit_of_round(r, units);
+        if (idx < 0) break;
+        const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
+        if (un.kt_vis == un.kt0) continue;
+        const int qb = j & 1;
+        if (!mbar_wait(qfull_bar(qb), (j >> 1) & 1, abort_flag, (KID_INDEX << 16) | 2)) break;
+        const uint32_t q_addr = sQ + qb * C::kQBytes;
+        for (int kt = un.kt0; kt < un.kt_vis; ++kt, ++i) {
+          const uint32_t buf = i & 1u;
+          if (!mbar_wait(tempty_bar(buf), (i >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 3) ||
+              !mbar_wait(kfull_bar(stage), phase, abort_flag, (KID_INDEX << 16) | 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t k_addr = sK + stage * C::kKBytes;
+          const uint32_t d_tmem = tmem_base + buf * kNmma;
 #pragma unroll
-        for (int k = 0; k < D / 32; ++k) {
-          umma_i8(d_tmem, make_sdesc(k_addr + 32 * k, D), make_sdesc(sQ + 32 * k, D), idesc, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 32; ++k) {
+            umma_i8(d_tmem, make_sdesc(k_addr + 32 * k, D), make_sdesc(q_addr + 32 * k, D), idesc, k > 0 ? 1u : 0u);
+          }
+          umma_commit(kempty_bar(stage));
+          umma_commit(tfull_bar(buf));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        umma_commit(kempty_bar(stage));
-        umma_commit(tfull_bar(buf));
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        umma_commit(qempty_bar(qb));  // the Q buffer is free once this unit's MMAs are done
+        ++j;
       }
       umma_commit(mma_done_bar);
       drain_wait(mma_done_bar, 0);
+    }
+  } else if (warp >= kFillWarp0) {
+    // ------------------------------------------------------------ -inf for invisible key tiles
+    const int ft = threadIdx.x - kFillWarp0 * 32;  // 0..63
+    const bool vec4 = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+    for (int r = 0;; ++r) {
+      const int idx = unit_of_round(r, units);
+      if (idx < 0) break;
+      const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
+      if (un.kt_vis == un.kt1) continue;
+      const int n_lo = un.kt_vis * kKeysPerTile;
+      const int n_hi = min(N, un.kt1 * kKeysPerTile);
+      float* out_b = out + static_cast<int64_t>(un.b) * M * N;
+      for (int q = 0; q < C::QB; ++q) {
+        const int m = un.m0 + q;
+        if (m >= M) break;
+        float* row = out_b + static_cast<int64_t>(m) * N;
+        if (vec4) {  // n_lo is a multiple of 128 and rows are 16-byte aligned
+          float4* row4 = reinterpret_cast<float4*>(row);
+          const float4 ninf4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          for (int n4 = n_lo / 4 + ft; n4 < n_hi / 4; n4 += 64) row4[n4] = ninf4;
+          for (int n = (n_hi & ~3) + ft; n < n_hi; n += 64) row[n] = -INFINITY;
+        } else {
+          for (int n = n_lo + ft; n < n_hi; n += 64) row[n] = -INFINITY;
+        }
+      }
     }
   } else if (warp < kEpiWarps) {
     regs_inc<kEpiRegs>();
     // ------------------------------------------------------------ epilogue (256 threads)
     const int wq = warp & 3;
     const int wh = warp >> 2;
-    const int et = threadIdx.x;  // 0..255
-    // Head weights of the query block -> smem (rows past M read as 0).
-    for (int i = et; i < C::QB * H; i += kEpiWarps * 32) {
-      const int m = un.m0 + i / H;
-      sW[i] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (i % H)) : 0.f;
-    }
-    named_bar_sync(1, kEpiWarps * 32);
-
     const int q_first = wh * C::kQPerHalf;  // first query (within the block) of this half
     const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wh * C::kColsPerHalf);
-    float* out_b = out + static_cast<int64_t>(un.b) * M * N;
+    float* sWw = reinterpret_cast<float*>(smem + C::kOffW) + warp * C::kColsPerHalf;  // this warp's copy
+    const float4* w_half = reinterpret_cast<const float4*>(sWw);
     bool ok = true;
-
-    if (n_mma_tiles > 0) {
-      const float4* w_half = reinterpret_cast<const float4*>(sW + wh * C::kColsPerHalf);
-      __syncwarp();  // both accumulators start free
-      if (lane == 0) {
-        mbar_arrive(tempty_bar(0));
-        mbar_arrive(tempty_bar(1));
+    __syncwarp();  // both accumulators start free
+    if (lane == 0) {
+      mbar_arrive(tempty_bar(0));
+      mbar_arrive(tempty_bar(1));
+    }
+    uint32_t i = 0;
+    for (int r = 0; ok; ++r) {
+      const int idx = unit_of_round(r, units);
+      if (idx < 0) break;
+      const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
+      if (un.kt_vis == un.kt0) continue;
+      // Head weights of this half's queries (rows past M read as 0): a private copy per warp,
+      // so no barrier across warps is needed.
+      __syncwarp();
+      for (int e = lane; e < C::kColsPerHalf; e += 32) {
+        const int m = un.m0 + q_first + e / H;
+        sWw[e] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (e % H)) : 0.f;
       }
-      for (int i = 0; i < n_mma_tiles; ++i) {
-        const uint32_t buf = uint32_t(i) & 1u;
-        const int n = (un.kt0 + i) * kKeysPerTile + wq * 32 + lane;
+      __syncwarp();
+      float* out_b = out + static_cast<int64_t>(un.b) * M * N;
+      for (int kt = un.kt0; kt < un.kt_vis; ++kt, ++i) {
+        const uint32_t buf = i & 1u;
+        const int n = kt * kKeysPerTile + wq * 32 + lane;
         // k_s * 2^22 undoes the 2^-22 of the relu step (power-of-two scalings: same rounding).
         const float ks = (n < N) ? __ldg(k_s + static_cast<int64_t>(un.b) * N + n) * 0x1p22f : 0.f;
-        if (!mbar_wait_warp(tfull_bar(buf), (uint32_t(i) >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
+        if (!mbar_wait_warp(tfull_bar(buf), (i >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
           ok = false;
           break;
         }
@@ -253,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld32(ra);
 #pragma unroll
         for (int c = 0; c < C::kColsPerHalf / 32; ++c) {
-          uint32_t(&r)[32] = (c & 1) ? rb : ra;
+          uint32_t(&rr)[32] = (c & 1) ? rb : ra;
           uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
           if (c + 1 < C::kColsPerHalf / 32) tmem_ld32_async(tb + (c + 1) * 32, nxt);
 #pragma unroll
@@ -262,8 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int q = (c * 32 + 4 * j4) / H;   // query of these 4 columns (compile time)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int j = 4 * j4 + 2 * h;
-              const float2 v = make_float2(relu_i32_x2m22(r[j]), relu_i32_x2m22(r[j + 1]));
+              const int jj = 4 * j4 + 2 * h;
+              const float2 v = make_float2(relu_i32_x2m22(rr[jj]), relu_i32_x2m22(rr[jj + 1]));
               const float2 wv = h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
               acc[q] = __ffma2_rn(v, wv, acc[q]);
             }
@@ -282,19 +355,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (causal && static_cast<long long>(n) > start + m) sc = -INFINITY;
               out_b[static_cast<int64_t>(m) * N + n] = sc;
             }
-          }
-        }
-      }
-    }
-    // Tiles that no query of this block can see: -inf without loading or multiplying.
-    if (ok) {
-      for (int kt = un.kt_vis; kt < un.kt1; ++kt) {
-        const int n = kt * kKeysPerTile + wq * 32 + lane;
-        if (n < N) {
-#pragma unroll
-          for (int q = 0; q < C::kQPerHalf; ++q) {
-            const int m = un.m0 + q_first + q;
-            if (m < M) out_b[static_cast<int64_t>(m) * N + n] = -INFINITY;
           }
         }
       }

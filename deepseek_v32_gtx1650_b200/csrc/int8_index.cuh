@@ -13,13 +13,14 @@
 // every SM gets about the same number of tiles) and keeps its TMEM, barriers and pipelines across
 // units, so consecutive units overlap (the next unit's Q and key tiles load while the current
 // one is still in the epilogue).
-//   warp 8      TMA producer: the unit's Q block into one of two Q buffers, then its key tiles
-//               into a 4-stage ring.
-//   warp 9      MMA issuer: D / 32 MMAs per key tile into one of two int32 TMEM accumulators.
-//   warps 0-7   epilogue: each thread owns one key and reduces relu(logit) * w over the heads of
+//   warps 0-15  epilogue: each thread owns one key and reduces relu(logit) * w over the heads of
 //               its queries entirely in registers (no cross-lane reduction), then scales by k_s and
-//               stores. Warp w reads TMEM lanes 32*(w%4).. and the query half w/4 of the columns.
-//   warps 10-11 write -inf for the key tiles that no query of a unit can see (causal), which are
+//               stores. Warp w reads TMEM lanes 32*(w%4).. and column quarter w/4 (QB/4 queries);
+//               four epilogue warps per SM sub-partition hide the TMEM load latency.
+//   warp 16     TMA producer: the unit's Q block into one of two Q buffers, then its key tiles
+//               into a 4-stage ring.
+//   warp 17     MMA issuer: D / 32 MMAs per key tile into one of two int32 TMEM accumulators.
+//   warps 18-19 write -inf for the key tiles that no query of a unit can see (causal), which are
 //               neither loaded nor multiplied (the reference's tile skip, kernels.py:145-148).
 //
 // Per logit: relu and the int32 -> fp32 conversion in one saturating fp32 multiply of the raw bits
@@ -36,13 +37,13 @@ namespace index {
 
 constexpr int kKeysPerTile = 128;
 constexpr int kStages = 4;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
 constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 -inf writers
-// Launch: 384 threads x 168 registers = 64512. setmaxnreg moves them to the epilogue:
-// 2 warpgroups x 128 x 200 + 1 warpgroup x 128 x 104 = 64512 (and per sub-partition
-// 200 + 200 + 104 = 504 <= 512).
-constexpr uint32_t kEpiRegs = 200;
-constexpr uint32_t kCtlRegs = 104;
+// Launch: 640 threads x 96 registers = 61440. setmaxnreg moves them to the epilogue:
+// 4 warpgroups x 128 x 104 + 1 warpgroup x 128 x 64 = 61440 (and per sub-partition
+// 4 x 104 + 64 = 480 <= 512).
+constexpr uint32_t kEpiRegs = 104;
+constexpr uint32_t kCtlRegs = 64;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kFillWarp0 = kEpiWarps + 2;
@@ -53,12 +54,12 @@ struct Cfg {
   static constexpr int QB = kNmma / H;                 // queries per block
   static constexpr int kQBytes = QB * H * D;           // Q tile bytes
   static constexpr int kKBytes = kKeysPerTile * D;     // key tile bytes per stage
-  static constexpr int kColsPerHalf = kNmma / 2;       // columns per epilogue warpgroup
-  static constexpr int kQPerHalf = QB / 2;
+  static constexpr int kColsPerWarp = kNmma / 4;      // columns per epilogue warp (one quarter)
+  static constexpr int kQPerWarp = QB / 4;            // queries per epilogue warp
   static constexpr int kOffQ = 0;                      // two Q buffers
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffW = kOffK + kStages * kKBytes;  // per epilogue warp: its half's weights
-  static constexpr int kOffBar = kOffW + kEpiWarps * kColsPerHalf * 4;
+  static constexpr int kOffBar = kOffW + kEpiWarps * kColsPerWarp * 4;
   // qfull[2], qempty[2], kfull[kStages], kempty[kStages], tfull[2], tempty[2], mma_done
   static constexpr int kNumBars = 9 + 2 * kStages;
   static constexpr int kOffTmem = kOffBar + 8 * kNumBars;
@@ -67,7 +68,7 @@ struct Cfg {
   static constexpr int kAlloc = kBytes + 1024;
   static_assert(QB * H == kNmma, "QB*H must be 256");
   static_assert(D == 64 || D == 128, "head dim must be 64 or 128");
-  static_assert(QB % 2 == 0, "two query halves");
+  static_assert(QB % 4 == 0, "four query quarters");
 };
 
 DSV32_DEV void drain_wait(uint32_t bar, uint32_t parity) {
@@ -278,13 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kEpiWarps) {
     regs_inc<kEpiRegs>();
-    // ------------------------------------------------------------ epilogue (256 threads)
-    const int wq = warp & 3;
-    const int wh = warp >> 2;
-    const int q_first = wh * C::kQPerHalf;  // first query (within the block) of this half
-    const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wh * C::kColsPerHalf);
-    float* sWw = reinterpret_cast<float*>(smem + C::kOffW) + warp * C::kColsPerHalf;  // this warp's copy
-    const float4* w_half = reinterpret_cast<const float4*>(sWw);
+    // ------------------------------------------------------------ epilogue (512 threads)
+    const int wq = warp & 3;   // TMEM lane quarter (keys)
+    const int wc = warp >> 2;  // column quarter (queries)
+    const int q_first = wc * C::kQPerWarp;  // first query (within the block) of this warp
+    const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wc * C::kColsPerWarp);
+    float* sWw = reinterpret_cast<float*>(smem + C::kOffW) + warp * C::kColsPerWarp;  // this warp's copy
+    const float4* w4p = reinterpret_cast<const float4*>(sWw);
     bool ok = true;
     __syncwarp();  // both accumulators start free
     if (lane == 0) {
@@ -297,10 +298,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (idx < 0) break;
       const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
       if (un.kt_vis == un.kt0) continue;
-      // Head weights of this half's queries (rows past M read as 0): a private copy per warp,
+      // Head weights of this warp's queries (rows past M read as 0): a private copy per warp,
       // so no barrier across warps is needed.
       __syncwarp();
-      for (int e = lane; e < C::kColsPerHalf; e += 32) {
+      for (int e = lane; e < C::kColsPerWarp; e += 32) {
         const int m = un.m0 + q_first + e / H;
         sWw[e] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (e % H)) : 0.f;
       }
@@ -316,42 +317,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float2 acc[C::kQPerHalf];
-#pragma unroll
-        for (int q = 0; q < C::kQPerHalf; ++q) acc[q] = make_float2(0.f, 0.f);
-        // TMEM reads are software-pipelined: chunk c+1 is in flight while chunk c is reduced.
+        // Both 32-column chunks of this warp's quarter in flight at once, then one wait.
         const uint32_t tb = t_lane + buf * kNmma;
         uint32_t ra[32], rb[32];
         tmem_ld32_async(tb, ra);
+        tmem_ld32_async(tb + 32, rb);
         tmem_wait_ld32(ra);
-#pragma unroll
-        for (int c = 0; c < C::kColsPerHalf / 32; ++c) {
-          uint32_t(&rr)[32] = (c & 1) ? rb : ra;
-          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-          if (c + 1 < C::kColsPerHalf / 32) tmem_ld32_async(tb + (c + 1) * 32, nxt);
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 w4 = w_half[c * 8 + j4];  // same address across the warp: broadcast
-            const int q = (c * 32 + 4 * j4) / H;   // query of these 4 columns (compile time)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int jj = 4 * j4 + 2 * h;
-              const float2 v = make_float2(relu_i32_x2m22(rr[jj]), relu_i32_x2m22(rr[jj + 1]));
-              const float2 wv = h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
-              acc[q] = __ffma2_rn(v, wv, acc[q]);
-            }
-          }
-          if (c + 1 < C::kColsPerHalf / 32) tmem_wait_ld32(nxt);
-        }
+        tmem_wait_ld32(rb);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar(buf));
+        if (lane == 0) mbar_arrive(tempty_bar(buf));  // the accumulator is in registers now
+        // Two accumulators per query (even / odd column pairs) halve the FMA dependency chain.
+        float2 acc[C::kQPerWarp][2];
+#pragma unroll
+        for (int q = 0; q < C::kQPerWarp; ++q) acc[q][0] = acc[q][1] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t(&rr)[32] = c ? rb : ra;
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 w4 = w4p[c * 8 + j4];     // same address across the warp: broadcast
+            const int q = (c * 32 + 4 * j4) / H;  // query of these 4 columns (compile time)
+            const float2 v0 = make_float2(relu_i32_x2m22(rr[4 * j4]), relu_i32_x2m22(rr[4 * j4 + 1]));
+            const float2 v1 = make_float2(relu_i32_x2m22(rr[4 * j4 + 2]), relu_i32_x2m22(rr[4 * j4 + 3]));
+            acc[q][0] = __ffma2_rn(v0, make_float2(w4.x, w4.y), acc[q][0]);
+            acc[q][1] = __ffma2_rn(v1, make_float2(w4.z, w4.w), acc[q][1]);
+          }
+        }
         if (n < N) {
 #pragma unroll
-          for (int q = 0; q < C::kQPerHalf; ++q) {
+          for (int q = 0; q < C::kQPerWarp; ++q) {
             const int m = un.m0 + q_first + q;
             if (m < M) {
-              float sc = (acc[q].x + acc[q].y) * ks;
+              float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
               if (causal && static_cast<long long>(n) > start + m) sc = -INFINITY;
               out_b[static_cast<int64_t>(m) * N + n] = sc;
             }

@@ -44,6 +44,11 @@ constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MM
 // 216 + 216 + 72 = 504 <= 512).
 constexpr uint32_t kEpiRegs = 216;
 constexpr uint32_t kCtlRegs = 72;
+// setmaxnreg.inc draws on the registers the CTA was launched with, not on the SM's file: the
+// split must fit the launch total or the increasing warps wait forever.
+constexpr int kLaunchRegs = 168;  // __launch_bounds__(384, 1): 65536 / 384 rounded down to 8
+static_assert(kEpiRegs * kEpiWarps * 32 + kCtlRegs * 4 * 32 <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 

@@ -20,7 +20,7 @@
 //   warp 16     TMA producer: the unit's Q block into one of two Q buffers, then its key tiles
 //               into a 4-stage ring.
 //   warp 17     MMA issuer: D / 32 MMAs per key tile into one of two int32 TMEM accumulators.
-//   warps 18-19 write -inf for the key tiles that no query of a unit can see (causal), which are
+//   warp 18     writes -inf for the key tiles that no query of a unit can see (causal), which are
 //               neither loaded nor multiplied (the reference's tile skip, kernels.py:145-148).
 //
 // Per logit: relu and the int32 -> fp32 conversion in one saturating fp32 multiply of the raw bits
@@ -38,15 +38,12 @@ namespace index {
 constexpr int kKeysPerTile = 128;
 constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;
-constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 -inf writers
-// Launch: 640 threads x 96 registers = 61440. setmaxnreg moves them to the epilogue:
-// 4 warpgroups x 128 x 104 + 1 warpgroup x 128 x 64 = 61440 (and per sub-partition
-// 4 x 104 + 64 = 480 <= 512).
-constexpr uint32_t kEpiRegs = 104;
-constexpr uint32_t kCtlRegs = 64;
+constexpr int kThreads = (kEpiWarps + 3) * 32;  // + producer, MMA and one -inf writer warp
+// 608 threads x 104 registers = 63232 of the SM's 65536; no register re-balancing (the warps do
+// not form whole warpgroups past the epilogue, and 104 is what the epilogue needs).
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
-constexpr int kFillWarp0 = kEpiWarps + 2;
+constexpr int kFillWarp = kEpiWarps + 2;
 constexpr int kNmma = 256;  // QB * H
 
 template <int H, int D>
@@ -163,9 +160,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp >= kEpiWarps) {
-    regs_dec<kCtlRegs>();
-  }
   if (warp == kProducerWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -251,9 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(mma_done_bar);
       drain_wait(mma_done_bar, 0);
     }
-  } else if (warp >= kFillWarp0) {
+  } else if (warp == kFillWarp) {
     // ------------------------------------------------------------ -inf for invisible key tiles
-    const int ft = threadIdx.x - kFillWarp0 * 32;  // 0..63
+    const int ft = lane;
     const bool vec4 = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
     for (int r = 0;; ++r) {
       const int idx = unit_of_round(r, units);
@@ -270,15 +264,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (vec4) {  // n_lo is a multiple of 128 and rows are 16-byte aligned
           float4* row4 = reinterpret_cast<float4*>(row);
           const float4 ninf4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          for (int n4 = n_lo / 4 + ft; n4 < n_hi / 4; n4 += 64) row4[n4] = ninf4;
-          for (int n = (n_hi & ~3) + ft; n < n_hi; n += 64) row[n] = -INFINITY;
+          for (int n4 = n_lo / 4 + ft; n4 < n_hi / 4; n4 += 32) row4[n4] = ninf4;
+          for (int n = (n_hi & ~3) + ft; n < n_hi; n += 32) row[n] = -INFINITY;
         } else {
-          for (int n = n_lo + ft; n < n_hi; n += 64) row[n] = -INFINITY;
+          for (int n = n_lo + ft; n < n_hi; n += 32) row[n] = -INFINITY;
         }
       }
     }
   } else if (warp < kEpiWarps) {
-    regs_inc<kEpiRegs>();
     // ------------------------------------------------------------ epilogue (512 threads)
     const int wq = warp & 3;   // TMEM lane quarter (keys)
     const int wc = warp >> 2;  // column quarter (queries)

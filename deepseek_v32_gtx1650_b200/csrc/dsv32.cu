@@ -292,8 +292,11 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
   return DSV32_ERR_UNSUPPORTED;
 }
 
+// causal_m > 0: row r (= b * causal_m + m) has its scores past key causal_start + m masked to -inf
+// (the indexer's causal rows); those positions are treated as -inf without being read.
 int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
-              int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
+              int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream, int64_t causal_m = 0,
+              int64_t causal_start = 0) {
   if (!scores || !out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
   if (rows < 1 || n < 1 || k < 1 || k > n || ld < n) return DSV32_ERR_INVALID_ARG;
   if (cand_idx && cand_ld < n) return DSV32_ERR_INVALID_ARG;
@@ -305,12 +308,16 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   using namespace dsv32::topk;
   const unsigned g = static_cast<unsigned>(rows);
   const int nn = static_cast<int>(n), kk = static_cast<int>(k);
+  const int cm = causal_m > 0 && causal_m <= 0x7FFFFFFFLL ? static_cast<int>(causal_m) : 0;
   if (n <= 256 * 4) {
-    topk_reg_kernel<256, 4><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+    topk_reg_kernel<256, 4><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val,
+                                                 cm, static_cast<long long>(causal_start));
   } else if (n <= 256 * 16) {
-    topk_reg_kernel<256, 16><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+    topk_reg_kernel<256, 16><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val,
+                                                 cm, static_cast<long long>(causal_start));
   } else if (n <= 512 * 16) {
-    topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+    topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val,
+                                                 cm, static_cast<long long>(causal_start));
   } else {
     topk_gmem_kernel<1024><<<g, 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
   }
@@ -438,11 +445,12 @@ int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const i
 
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,
                           int64_t batch, int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start,
-                          int64_t topk, int32_t* out_idx, float* out_val, void* stream) {
+                          int64_t topk, int64_t key_offset, int32_t* out_idx, float* out_val, void* stream) {
   if (topk < 1 || topk > n) return DSV32_ERR_INVALID_ARG;
   if (!out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
   if (int st = index_impl(q, w, k, k_s, scores, batch, m, n, heads, dim, causal, start, stream)) return st;
-  return topk_impl(scores, batch * m, n, n, nullptr, 0, 0, topk, out_idx, out_val, stream);
+  return topk_impl(scores, batch * m, n, n, nullptr, 0, key_offset, topk, out_idx, out_val, stream, causal ? m : 0,
+                   start);
 }
 
 int dsv32_device_status(int device, uint32_t* code) {

@@ -17,7 +17,11 @@
 //     three passes), each pass counting only keys that match the prefix found so far.
 //  3. Ordered compaction: block-wide prefix sums over per-thread contiguous chunks place every
 //     key > T and the first k_rem keys == T in position order.
-// topk_reg_kernel keeps a row of up to THREADS*ITEMS keys in registers (one read of the row);
+// topk_reg_kernel keeps a row of up to THREADS*ITEMS keys in registers (one read of the row),
+// gathers the statistics of step 1 behind a single barrier, and as soon as the open histogram bin
+// holds at most THREADS keys it ranks those keys directly instead of running further passes; the
+// selected entries are staged in shared memory and written with 16-byte stores. For causal indexer
+// rows the masked tail is known and is counted as -inf without being read.
 // topk_gmem_kernel re-reads longer rows from global memory (L2) in each pass.
 #pragma once
 #include "common.cuh"
@@ -140,19 +144,77 @@ DSV32_DEV void pick_digit(SelShared& sh, int nbins, int shift, uint32_t prefix, 
 }
 
 // ---------------------------------------------------------------------------- register rows
+constexpr int kRegBits = 11;                // digit width of the register kernel's histograms
+constexpr int kRegBins = 1 << kRegBits;
+constexpr int kStageMax = 2048;             // outputs staged in shared memory (16-byte stores) up to this k
+
+template <int THREADS>
+struct RegShared {
+  union {
+    alignas(16) int hist[kRegBins];
+    struct {
+      int32_t idx[kStageMax];
+      float val[kStageMax];
+    } out;
+  } u;
+  uint32_t cand[32];       // keys of the last open histogram bin (at most 32)
+  uint32_t red[4][32];     // per-warp partial statistics
+  int scan[32];
+  uint32_t prefix, T;
+  int krem, bin_cnt, cand_n;
+};
+
+// Visible length of a row: positions >= valid are -inf without being read (causal rows of the
+// indexer, whose masked tail is known). causal_m == 0: the whole row.
+DSV32_DEV int row_valid(long long row, int n, int causal_m, long long causal_start) {
+  if (causal_m <= 0) return n;
+  const long long v = causal_start + (row % causal_m) + 1;
+  return static_cast<int>(v < 0 ? 0 : (v > n ? n : v));
+}
+
+// Block-wide exclusive prefix sum (thread order) with a single barrier.
+template <int THREADS>
+DSV32_DEV int excl_scan_once(int v, int* buf) {
+  constexpr int W = THREADS / 32;
+  const int lane = threadIdx.x & 31;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) buf[threadIdx.x >> 5] = incl;
+  __syncthreads();
+  int before = 0;
+  const int wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < W; ++i) before += (i < wid) ? buf[i] : 0;
+  return before + incl - v;
+}
+
+// Positions past n hold key 0 (below every real key except the all-ones negative NaN): they never
+// count as above -inf, never reach a histogram while the floor is above -inf, and never equal a
+// threshold >= the -inf key. Only the negative-NaN path (threshold below -inf) checks positions.
 template <int THREADS, int ITEMS>
 __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restrict__ vals, long long ld, int n,
                                                            const int32_t* __restrict__ cand_idx, long long cand_ld,
                                                            long long idx_offset, int k, int32_t* __restrict__ out_idx,
-                                                           float* __restrict__ out_val) {
-  __shared__ SelShared sh;
-  int parity = 0;
+                                                           float* __restrict__ out_val, int causal_m,
+                                                           long long causal_start) {
+  constexpr int W = THREADS / 32;
+  __shared__ RegShared<THREADS> sh;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int wid = tid >> 5;
   const long long row = blockIdx.x;
   const float* v = vals + row * ld;
-  const int pos0 = threadIdx.x * ITEMS;
+  const int valid = row_valid(row, n, causal_m, causal_start);
+  const int pos0 = tid * ITEMS;
+  for (int i = tid; i < kRegBins; i += THREADS) sh.u.hist[i] = 0;  // first radix pass
   uint32_t key[ITEMS];
-  // Each thread owns ITEMS consecutive positions (position order = thread order).
-  if ((ld & 3) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && (ITEMS % 4) == 0 && pos0 + ITEMS <= n) {
+  // Each thread owns ITEMS consecutive positions (position order = thread order). Positions in
+  // [valid, n) are -inf without a read.
+  if ((ld & 3) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && (ITEMS % 4) == 0 && pos0 + ITEMS <= valid) {
 #pragma unroll
     for (int i = 0; i < ITEMS; i += 4) {
       const float4 f = __ldg(reinterpret_cast<const float4*>(v + pos0 + i));
@@ -163,86 +225,217 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) key[i] = (pos0 + i < n) ? fkey(__ldg(v + pos0 + i)) : 0u;
+    for (int i = 0; i < ITEMS; ++i)
+      key[i] = (pos0 + i < valid) ? fkey(__ldg(v + pos0 + i)) : (pos0 + i < n ? kNegInfKey : 0u);
   }
-  // 1. counts above / at the -inf key; range of the keys that take part in the histograms
-  int n_above = 0, n_ninf = 0;
-#pragma unroll
-  for (int i = 0; i < ITEMS; ++i) {
-    const bool valid = pos0 + i < n;
-    n_above += (valid && key[i] > kNegInfKey) ? 1 : 0;
-    n_ninf += (valid && key[i] == kNegInfKey) ? 1 : 0;
-  }
-  const int above = block_sum<THREADS>(n_above, sh.scratch, parity);
-  const int ninf = block_sum<THREADS>(n_ninf, sh.scratch, parity);
-  uint32_t T;
-  int k_rem;
-  if (above < k && above + ninf >= k) {
-    T = kNegInfKey;  // all values above -inf, then the lowest-position -inf entries
-    k_rem = k - above;
-  } else {
-    // 2. radix select among keys >= floor (above -inf; or every key if negative NaNs are needed)
-    const uint32_t floor_key = (above >= k) ? kNegInfKey + 1u : 0u;
+  // 1. Row statistics behind one barrier (which also orders the histogram clear before pass 1):
+  //    counts above / at the -inf key and the key range of the values above -inf.
+  {
+    int na = 0, ni = 0;
     uint32_t mn = 0xFFFFFFFFu, mx = 0u;
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
-      const bool part = pos0 + i < n && key[i] >= floor_key;
-      mn = part ? min(mn, key[i]) : mn;
-      mx = part ? max(mx, key[i]) : mx;
+      const bool a = key[i] > kNegInfKey;
+      na += a ? 1 : 0;
+      ni += key[i] == kNegInfKey ? 1 : 0;
+      mn = a ? min(mn, key[i]) : mn;
+      mx = a ? max(mx, key[i]) : mx;
     }
-    block_minmax<THREADS>(mn, mx, sh.mm, parity);
-    int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);  // bits [shift, 32) common to every participant
-    uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
-    k_rem = k;
-    while (shift > 0) {
-      const int d = min(kHistBits, shift);
-      const int nbins = 1 << d;
-      for (int i = threadIdx.x; i < nbins; i += THREADS) sh.hist[i] = 0;
-      __syncthreads();
-      const int ns = shift - d;
+    const uint32_t r0 = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(na));
+    const uint32_t r1 = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(ni));
+    const uint32_t r2 = __reduce_min_sync(0xffffffffu, mn);
+    const uint32_t r3 = __reduce_max_sync(0xffffffffu, mx);
+    if (lane == 0) {
+      sh.red[0][wid] = r0;
+      sh.red[1][wid] = r1;
+      sh.red[2][wid] = r2;
+      sh.red[3][wid] = r3;
+    }
+  }
+  __syncthreads();
+  int above = 0, ninf = 0;
+  uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    above += static_cast<int>(sh.red[0][w]);
+    ninf += static_cast<int>(sh.red[1][w]);
+    mn = min(mn, sh.red[2][w]);
+    mx = max(mx, sh.red[3][w]);
+  }
+  uint32_t T;
+  int krem;
+  if (above < k && above + ninf >= k) {
+    T = kNegInfKey;  // all values above -inf, then the lowest-position -inf entries
+    krem = k - above;
+  } else {
+    // 2. Radix select among the participating keys: those above -inf, or (negative NaNs needed,
+    //    never for indexer scores) every real position.
+    const bool nan_path = above < k;
+    uint32_t floor_key = kNegInfKey + 1u;
+    if (nan_path) {
+      floor_key = 0u;
+      mn = 0xFFFFFFFFu;
+      mx = 0u;
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) {
-        const bool part = pos0 + i < n && key[i] >= floor_key && prefix_match(key[i], prefix, shift);
-        if (part) atomicAdd(&sh.hist[(key[i] >> ns) & (nbins - 1)], 1);
+        if (pos0 + i < n) {
+          mn = min(mn, key[i]);
+          mx = max(mx, key[i]);
+        }
+      }
+      mn = __reduce_min_sync(0xffffffffu, mn);
+      mx = __reduce_max_sync(0xffffffffu, mx);
+      if (lane == 0) {
+        sh.red[2][wid] = mn;
+        sh.red[3][wid] = mx;
       }
       __syncthreads();
-      pick_digit<THREADS>(sh, nbins, ns, prefix, k_rem, parity);
-      prefix = sh.prefix;
-      k_rem = sh.krem;
-      shift = ns;
-      __syncthreads();
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        mn = min(mn, sh.red[2][w]);
+        mx = max(mx, sh.red[3][w]);
+      }
     }
-    T = prefix;
+    int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);  // bits [shift, 32) common to every participant
+    uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
+    krem = k;
+    bool first = true, resolved = false;
+    while (shift > 0) {
+      const int d = min(kRegBits, shift);
+      const int nbins = 1 << d;
+      const int ns = shift - d;
+      if (!first) {
+        for (int i = tid; i < nbins; i += THREADS) sh.u.hist[i] = 0;
+        __syncthreads();
+      }
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) {
+        const bool part = nan_path ? (pos0 + i < n) : (key[i] >= floor_key);
+        if (part && (first || prefix_match(key[i], prefix, shift)))
+          atomicAdd(&sh.u.hist[(key[i] >> ns) & (nbins - 1)], 1);
+      }
+      first = false;
+      __syncthreads();
+      // The digit holding the krem-th largest participating key: bins in descending order,
+      // `per` consecutive bins per thread (read as 16-byte vectors: no bank conflicts).
+      const int per = (nbins + THREADS - 1) / THREADS;
+      int local = 0;
+      if ((per & 3) == 0) {
+        const int4* hv = reinterpret_cast<const int4*>(sh.u.hist + (nbins - (tid + 1) * per));
+        for (int j = 0; j < per / 4; ++j) {
+          const int4 h4 = hv[j];
+          local += (h4.x + h4.y) + (h4.z + h4.w);
+        }
+      } else {
+        for (int j = 0; j < per; ++j) {
+          const int bin = nbins - 1 - (tid * per + j);
+          if (bin >= 0) local += sh.u.hist[bin];
+        }
+      }
+      const int before = excl_scan_once<THREADS>(local, sh.scan);
+      if (before < krem && krem <= before + local) {
+        int acc = before;
+        for (int j = 0; j < per; ++j) {
+          const int bin = nbins - 1 - (tid * per + j);
+          const int c = sh.u.hist[bin];
+          if (acc + c >= krem) {
+            sh.prefix = prefix | (uint32_t(bin) << ns);
+            sh.krem = krem - acc;
+            sh.bin_cnt = c;
+            sh.cand_n = 0;
+            break;
+          }
+          acc += c;
+        }
+      }
+      __syncthreads();  // also separates this pass's histogram reads from the next clear
+      prefix = sh.prefix;
+      krem = sh.krem;
+      const int cnt = sh.bin_cnt;
+      shift = ns;
+      if (shift > 0 && cnt <= 32) {
+        // At most a warp's worth of keys share the digits found so far: one warp ranks them
+        // (register shuffles) instead of running more passes.
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+          const bool part = nan_path ? (pos0 + i < n) : (key[i] >= floor_key);
+          if (part && prefix_match(key[i], prefix, shift)) sh.cand[atomicAdd(&sh.cand_n, 1)] = key[i];
+        }
+        __syncthreads();
+        if (wid == 0) {
+          const uint32_t mine = lane < cnt ? sh.cand[lane] : 0u;
+          int g = 0, e = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const uint32_t c = __shfl_sync(0xffffffffu, mine, j);
+            g += (j < cnt && c > mine) ? 1 : 0;
+            e += (j < cnt && c == mine) ? 1 : 0;
+          }
+          if (lane < cnt && g < krem && krem <= g + e) {  // every holder of this key writes the same values
+            sh.T = mine;
+            sh.krem = krem - g;
+          }
+        }
+        __syncthreads();
+        T = sh.T;
+        krem = sh.krem;
+        resolved = true;
+        break;
+      }
+    }
+    if (!resolved) T = prefix;
   }
-  // 3. ordered compaction
+  // 3. Ordered compaction: one scan of (greater, equal) counts gives every thread its output slot.
+  const bool check_pos = T < kNegInfKey;  // only a negative-NaN threshold can equal the padding key
   int gt = 0, eq = 0;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
-    if (pos0 + i < n) {
-      gt += key[i] > T ? 1 : 0;
-      eq += key[i] == T ? 1 : 0;
-    }
+    const bool real = !check_pos || pos0 + i < n;
+    gt += (key[i] > T && real) ? 1 : 0;
+    eq += (key[i] == T && real) ? 1 : 0;
   }
-  const int eq_before = block_excl_scan<THREADS>(eq, sh.scratch, parity);
-  const int take_eq = max(0, min(eq, k_rem - eq_before));
-  int o = block_excl_scan<THREADS>(gt + take_eq, sh.scratch, parity);
+  const int packed = excl_scan_once<THREADS>((gt << 16) | eq, sh.scan);  // n <= 65535
+  const int eq_before = packed & 0xFFFF;
+  int o = (packed >> 16) + min(eq_before, krem);
   const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld : nullptr;
   int32_t* oi = out_idx + row * k;
   float* ov = out_val + row * k;
+  const bool staged = k <= kStageMax;
   int e = eq_before;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const int pos = pos0 + i;
-    if (pos < n) {
-      bool sel = key[i] > T;
-      if (key[i] == T) {
-        sel = e < k_rem;
-        ++e;
+    const bool real = !check_pos || pos < n;
+    bool sel = key[i] > T && real;
+    if (key[i] == T && real) {
+      sel = e < krem;
+      ++e;
+    }
+    if (sel) {
+      const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + idx_offset);
+      const float x = fkey_inv(key[i]);
+      if (staged) {
+        sh.u.out.idx[o] = id;
+        sh.u.out.val[o] = x;
+      } else {
+        oi[o] = id;
+        ov[o] = x;
       }
-      if (sel) {
-        oi[o] = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + idx_offset);
-        ov[o] = fkey_inv(key[i]);
-        ++o;
+      ++o;
+    }
+  }
+  if (staged) {
+    __syncthreads();
+    if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(out_idx) & 15u) == 0 &&
+        (reinterpret_cast<uintptr_t>(out_val) & 15u) == 0) {
+      for (int j = tid; j < k / 4; j += THREADS) {
+        reinterpret_cast<int4*>(oi)[j] = reinterpret_cast<const int4*>(sh.u.out.idx)[j];
+        reinterpret_cast<float4*>(ov)[j] = reinterpret_cast<const float4*>(sh.u.out.val)[j];
+      }
+    } else {
+      for (int j = tid; j < k; j += THREADS) {
+        oi[j] = sh.u.out.idx[j];
+        ov[j] = sh.u.out.val[j];
       }
     }
   }

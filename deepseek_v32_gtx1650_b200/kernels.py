@@ -192,9 +192,8 @@ def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_score
         lib = _lib.load()
         with _OnDevice(q):
             s = _stream(q)
-            _lib.check(lib.dsv32_int8_index(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
-                                            scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start), s),
+            _lib.check(lib.dsv32_int8_index_topk(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
+                                                 scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start),
+                                                 topk, int(key_offset), idx.data_ptr(), vals.data_ptr(), s),
                        "int8_index_topk")
-            _lib.check(lib.dsv32_topk(scores.data_ptr(), B * M, Nk, Nk, None, 0, int(key_offset), topk,
-                                      idx.data_ptr(), vals.data_ptr(), s), "int8_index_topk")
     return (scores, idx, vals) if return_scores else (idx, vals)

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define DSV32_ABI_VERSION 2
+#define DSV32_ABI_VERSION 3
 
 /* Status codes. */
 #define DSV32_OK 0
@@ -111,11 +111,13 @@ int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const i
 
 /* Indexer + top-k in one call (bench_indexer_e2e.py:54-57,72-77): scores are written to the
  * caller's `scores` buffer [batch, m, n] fp32 (workspace; it also holds the full scores on return),
- * then the top `topk` keys of every (batch, query) row are selected as dsv32_topk does.
+ * then the top `topk` keys of every (batch, query) row are selected as dsv32_topk does, with
+ * index = key position + key_offset (a key shard's first global key; 0 for a whole cache).
+ * With causal != 0 the selection does not re-read the masked tail of each row.
  * out_idx / out_val [batch, m, topk]. Requires 1 <= topk <= n. */
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,
                           int64_t batch, int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start,
-                          int64_t topk, int32_t* out_idx, float* out_val, void* stream);
+                          int64_t topk, int64_t key_offset, int32_t* out_idx, float* out_val, void* stream);
 
 /* Synchronises `device`, then reads and clears its kernel error word. *code = 0 if no kernel
  * gave up on an internal wait since the last call; else (kernel_id << 16) | site. Returns

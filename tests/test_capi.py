@@ -38,7 +38,7 @@ def test_library_builds_and_exports_every_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.dsv32_abi_version() == 2
+    assert lib.dsv32_abi_version() == 3
     for code in range(6):
         assert lib.dsv32_status_string(code)
     assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")
@@ -60,7 +60,7 @@ def test_argument_validation_without_gpu():
         _lib.DSV32_ERR_UNSUPPORTED
     assert lib.dsv32_topk(fake, 4, 100, 100, None, 0, 0, 101, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_int8_gemm_workspace_bytes(4, 100, 128) == -_lib.DSV32_ERR_UNSUPPORTED
-    assert lib.dsv32_int8_index_topk(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 0, fake, fake,
+    assert lib.dsv32_int8_index_topk(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 0, 0, fake, fake,
                                      None) == _lib.DSV32_ERR_INVALID_ARG
     # misaligned operand
     odd = ctypes.c_void_p(4096 + 4)

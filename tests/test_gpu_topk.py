@@ -103,3 +103,19 @@ def test_select_topk_with_infinities():
     ri, rv = O.topk_ref(s.numpy(), 2048)
     np.testing.assert_array_equal(npy(idx), ri)
     np.testing.assert_array_equal(npy(vals), rv)
+
+
+@pytest.mark.parametrize("start", [-300, 0, 700])
+def test_index_topk_causal_batched_with_offset(start):
+    """The fused call skips reading each causal row's masked tail; its selection must equal the
+    deterministic top-k of the scores it returns, for every batch and a shifted causal start."""
+    B, M, N, topk = 2, 384, 1536, 512
+    q, w, k, ks = workloads.index_inputs(B, M, N, seed=11)
+    scores, idx, vals = D.int8_index_topk(q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV), topk=topk, causal=True,
+                                          start=start, key_offset=4096)
+    for b in range(B):
+        sc = npy(scores)[b]
+        ri, rv = O.topk_ref(sc, topk)
+        np.testing.assert_array_equal(npy(idx)[b], ri + 4096)
+        np.testing.assert_array_equal(npy(vals)[b], rv)
+    assert_no_device_error()

@@ -14,6 +14,11 @@
 // 16 (bf16/fp16) or 32 (fp32) lanes; amax by xor-shuffles inside that lane group. Each
 // warp handles UNROLL consecutive group-slots per iteration so several 16-byte loads
 // are in flight per lane (HBM latency hiding).
+//
+// Per value the work stays on the FP32 pipe: amax with a NaN-propagating max, the rounding as a
+// fused multiply-add with 1.5 * 2^23 whose result bits carry the int8 (aq_quant_bits), and byte
+// permutes to pack four results; no float -> int conversion instruction. Values within 2^-14 of a
+// rounding tie (about 1 in 8000) are recomputed with the IEEE division.
 #pragma once
 #include "common.cuh"
 
@@ -59,6 +64,21 @@ DSV32_DEV void to_f32(const uint4& v, float (&f)[8], __half*) {
   }
 }
 
+// max(a, b) that returns NaN when either input is NaN (torch.amax propagates NaN; fmaxf drops it).
+DSV32_DEV float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Reciprocal with at most 1 ulp of error (the PTX approximate reciprocal): enough for
+// aq_quant_bits, whose exactness argument allows 2^-23 relative error in r.
+DSV32_DEV float rcp_1ulp(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // fp32 scale from the group amax (already floored), both formats.
 DSV32_DEV float aq_scale(float amax, bool round_scale) {
   float s = amax * (1.0f / 127.0f);  // fl32(1/127) times fl32(amax), one fp32 rounding
@@ -74,16 +94,28 @@ DSV32_DEV float aq_scale(float amax, bool round_scale) {
   return s;
 }
 
-// round_half_even(x / s) for |x| <= amax, s = amax-derived scale (|x / s| <= 127 + tiny).
-// Exact fast path: q = x * rcp_rn(s) is within 2^-15 of fl(x / s) for |q| < 128 (two correctly rounded
-// steps, 2^-23 relative), so rint(q) == rint(fl(x / s)) unless q lies within 2^-14 of a half
-// integer; those (about 1 in 8000) take the IEEE division. NaN converts to 0.
-DSV32_DEV int aq_quant1(float x, float s, float r) {
-  const float q = x * r;
-  const float n = rintf(q);
-  float v = n;
-  if (fabsf(q - n) > 0.5f - 6.103515625e-05f) v = rintf(__fdiv_rn(x, s));  // near a tie
-  return __float2int_rn(v);  // |v| <= 127: no clamp needed
+// round_half_even(x / s) for |x| <= amax, s = amax-derived scale (|x / s| <= 127 + tiny), returned as
+// the fp32 bits of q + 1.5 * 2^23, whose low byte is q as a two's-complement int8. No conversion
+// instruction: fma(x, r, 1.5 * 2^23) rounds the exact product x * r once, to the nearest integer
+// (ties to even, since 1.5 * 2^23 is even and the float spacing there is 1). With r within 1 ulp
+// of 1/s, x * r is within 2^-16 + 2^-18 of fl(x / s) for |q| < 128 (2^-23 relative for r, half an
+// ulp for the quotient), so rint(x * r) == rint(fl(x / s)) unless x * r lies within 2^-14 of a half
+// integer; those (about 1 in 8000) and NaN products take the IEEE division. NaN converts to 0.
+DSV32_DEV uint32_t aq_quant_bits(float x, float s, float r) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float big = fmaf(x, r, kMagic);
+  const float n = big - kMagic;    // rint(x * r), exact
+  const float t = fmaf(x, r, -n);  // x * r - rint(x * r)
+  if (!(fabsf(t) <= 0.5f - 6.103515625e-05f)) {  // near a tie, or NaN
+    const float v = rintf(__fdiv_rn(x, s));
+    big = (v == v) ? v + kMagic : kMagic;
+  }
+  return __float_as_uint(big);
+}
+
+// Low bytes of four aq_quant_bits results, in order, as one 32-bit word.
+DSV32_DEV uint32_t aq_pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 template <typename T, int UNROLL>
@@ -102,58 +134,45 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
   const int64_t slots = (num_groups + GPW - 1) / GPW;
 
   for (int64_t base = warp * UNROLL; base < slots; base += nwarps * UNROLL) {
-    float f[UNROLL][EPL];
-    bool valid[UNROLL];
+    // All UNROLL 16-byte loads of the lane are issued before any is used; the raw vectors stay
+    // packed in registers until their group is processed.
+    uint4 raw[UNROLL];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int64_t g = (base + u) * GPW + sub;
-      valid[u] = (base + u) < slots && g < num_groups;
-      if (valid[u]) {
-        if constexpr (sizeof(T) == 4) {
-          const float4 v = __ldcs(reinterpret_cast<const float4*>(x + g * 128) + sl);
-          to_f32(v, reinterpret_cast<float(&)[4]>(f[u]));
-        } else {
-          const uint4 v = __ldcs(reinterpret_cast<const uint4*>(x + g * 128) + sl);
-          to_f32(v, reinterpret_cast<float(&)[8]>(f[u]), static_cast<T*>(nullptr));
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) f[u][e] = 0.f;
-      }
+      raw[u] = ((base + u) < slots && g < num_groups) ? __ldcs(reinterpret_cast<const uint4*>(x + g * 128) + sl)
+                                                      : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
-      float a = 0.f;
-      bool nan = false;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        a = fmaxf(a, fabsf(f[u][e]));
-        nan |= isnan(f[u][e]);
+      const int64_t g = (base + u) * GPW + sub;
+      const bool valid = (base + u) < slots && g < num_groups;
+      float f[EPL];
+      if constexpr (sizeof(T) == 4) {
+        to_f32(make_float4(__uint_as_float(raw[u].x), __uint_as_float(raw[u].y), __uint_as_float(raw[u].z),
+                           __uint_as_float(raw[u].w)),
+               reinterpret_cast<float(&)[4]>(f));
+      } else {
+        to_f32(raw[u], reinterpret_cast<float(&)[8]>(f), static_cast<T*>(nullptr));
       }
+      float a = 0.f;
 #pragma unroll
-      for (int o = LPG / 2; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-      // torch's amax propagates NaN while fmaxf drops it: detect NaN per group explicitly.
-      const unsigned nan_lanes = __ballot_sync(0xffffffffu, nan);
-      const unsigned group_lanes = (LPG == 32) ? 0xffffffffu : (0xFFFFu << (sub * 16));
-      float amax = fmaxf(a, 1e-4f);
-      if (nan_lanes & group_lanes) amax = __int_as_float(0x7fc00000);
+      for (int e = 0; e < EPL; ++e) a = max_nan(a, fabsf(f[e]));
+#pragma unroll
+      for (int o = LPG / 2; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
+      const float amax = max_nan(a, 1e-4f);  // NaN anywhere in the group -> NaN
       const float sc = aq_scale(amax, round_scale != 0);
-      const float rc = __frcp_rn(sc);
-      if (valid[u]) {
-        const int64_t g = (base + u) * GPW + sub;
+      const float rc = rcp_1ulp(sc);
+      if (valid) {
         if constexpr (EPL == 4) {
-          char4 q;
-          q.x = static_cast<int8_t>(aq_quant1(f[u][0], sc, rc));
-          q.y = static_cast<int8_t>(aq_quant1(f[u][1], sc, rc));
-          q.z = static_cast<int8_t>(aq_quant1(f[u][2], sc, rc));
-          q.w = static_cast<int8_t>(aq_quant1(f[u][3], sc, rc));
-          __stcs(reinterpret_cast<char4*>(y + g * 128) + sl, q);
+          const uint32_t w0 = aq_pack4(aq_quant_bits(f[0], sc, rc), aq_quant_bits(f[1], sc, rc),
+                                       aq_quant_bits(f[2], sc, rc), aq_quant_bits(f[3], sc, rc));
+          __stcs(reinterpret_cast<unsigned int*>(y + g * 128) + sl, w0);
         } else {
-          uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) w0 |= (uint32_t(uint8_t(aq_quant1(f[u][e], sc, rc))) << (8 * e));
-#pragma unroll
-          for (int e = 0; e < 4; ++e) w1 |= (uint32_t(uint8_t(aq_quant1(f[u][4 + e], sc, rc))) << (8 * e));
+          const uint32_t w0 = aq_pack4(aq_quant_bits(f[0], sc, rc), aq_quant_bits(f[1], sc, rc),
+                                       aq_quant_bits(f[2], sc, rc), aq_quant_bits(f[3], sc, rc));
+          const uint32_t w1 = aq_pack4(aq_quant_bits(f[4], sc, rc), aq_quant_bits(f[5], sc, rc),
+                                       aq_quant_bits(f[6], sc, rc), aq_quant_bits(f[7], sc, rc));
           __stcs(reinterpret_cast<uint2*>(y + g * 128) + sl, make_uint2(w0, w1));
         }
         if (sl == 0) s[g] = sc;

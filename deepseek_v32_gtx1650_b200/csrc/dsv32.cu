@@ -19,7 +19,9 @@
 
 namespace {
 
-constexpr int kAqUnroll = 4;  // 128-value groups in flight per warp slot per iteration
+// act_quant: 16-byte loads in flight per lane per iteration, by input width (fp32, 16-bit).
+constexpr int kAqUnrollF32 = 4;
+constexpr int kAqUnroll16 = 4;
 
 thread_local std::string t_last_error;
 
@@ -87,12 +89,12 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64>, index::Cfg<16, 64>::kAlloc));
       {
         int nb = 0;
-        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<float, kAqUnroll>, 256, 0));
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<float, kAqUnrollF32>, 256, 0));
         d.aq_blocks_per_sm[DSV32_F32] = nb > 0 ? nb : 1;
         DSV32_CUDA_TRY(
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__nv_bfloat16, kAqUnroll>, 256, 0));
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__nv_bfloat16, kAqUnroll16>, 256, 0));
         d.aq_blocks_per_sm[DSV32_BF16] = nb > 0 ? nb : 1;
-        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__half, kAqUnroll>, 256, 0));
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__half, kAqUnroll16>, 256, 0));
         d.aq_blocks_per_sm[DSV32_F16] = nb > 0 ? nb : 1;
       }
       if (!g_encode) {
@@ -358,24 +360,24 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
   DeviceInfo* info = nullptr;
   if (int st = device_setup(&dev, &info)) return st;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  constexpr int kUnroll = kAqUnroll;
+  using namespace dsv32;
+  const int unroll = (x_dtype == DSV32_F32) ? kAqUnrollF32 : kAqUnroll16;
   const int threads = 256;
   const int gpw = (x_dtype == DSV32_F32) ? 1 : 2;
   const int64_t slots = (groups + gpw - 1) / gpw;
-  const int64_t warps_needed = (slots + kUnroll - 1) / kUnroll;
+  const int64_t warps_needed = (slots + unroll - 1) / unroll;
   int64_t blocks = (warps_needed + (threads / 32) - 1) / (threads / 32);
   // One wave of resident CTAs, each looping over its share: no tail wave.
   const int64_t cap = static_cast<int64_t>(info->num_sms) * info->aq_blocks_per_sm[x_dtype];
   if (blocks > cap) blocks = cap;
-  using namespace dsv32;
   if (x_dtype == DSV32_F32) {
-    act_quant_kernel<float, kUnroll><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+    act_quant_kernel<float, kAqUnrollF32><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
         static_cast<const float*>(x), y, s, groups, round_scale);
   } else if (x_dtype == DSV32_BF16) {
-    act_quant_kernel<__nv_bfloat16, kUnroll><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+    act_quant_kernel<__nv_bfloat16, kAqUnroll16><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
         static_cast<const __nv_bfloat16*>(x), y, s, groups, round_scale);
   } else {
-    act_quant_kernel<__half, kUnroll><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+    act_quant_kernel<__half, kAqUnroll16><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
         static_cast<const __half*>(x), y, s, groups, round_scale);
   }
   return launch_check("act_quant_kernel launch");

@@ -82,3 +82,27 @@ def test_act_quant_empty_and_nan():
     _, sr = O.act_quant_ref(x.numpy())
     assert np.isnan(npy(s)[1, 0]) and np.isnan(sr[1, 0])  # NaN propagates to the group scale like torch.amax
     np.testing.assert_array_equal(npy(s)[0], sr[0])
+
+
+@pytest.mark.parametrize("dt,n", [(torch.float32, 2048), (torch.bfloat16, 4096), (torch.float16, 4096)])
+def test_act_quant_streaming_path_edge_cases(golden, dt, n):
+    """Inputs of 8 MB and more take the bulk-copy streaming kernel: an odd row count (uneven shares
+    and a partial last chunk), the adversarial ue8m0 groups, outliers, a zero group, NaN and inf."""
+    rows = 1031
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(rows, n, generator=g) * 2
+    x.view(-1)[::97] *= 50
+    adv = torch.from_numpy(adversarial_groups(golden["aq_adv_amax"])).float().reshape(-1)
+    x.view(-1)[: adv.numel()] = adv[: x.numel()]
+    x[5, :128] = 0
+    x[7, 300] = float("nan")
+    x[9, 1000] = float("inf")
+    x[11, 129] = float("-inf")
+    x = x.to(dt)
+    assert x.numel() * x.element_size() >= 8 << 20
+    for rs in (False, True):
+        y, s = D.act_quant(x.to(DEV), rs)
+        yr, sr = O.act_quant_ref(f32_of(x), rs)
+        np.testing.assert_array_equal(npy(s), sr)
+        np.testing.assert_array_equal(npy(y), yr)
+    assert_no_device_error()

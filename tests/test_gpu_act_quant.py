@@ -85,9 +85,9 @@ def test_act_quant_empty_and_nan():
 
 
 @pytest.mark.parametrize("dt,n", [(torch.float32, 2048), (torch.bfloat16, 4096), (torch.float16, 4096)])
-def test_act_quant_streaming_path_edge_cases(golden, dt, n):
-    """Inputs of 8 MB and more take the bulk-copy streaming kernel: an odd row count (uneven shares
-    and a partial last chunk), the adversarial ue8m0 groups, outliers, a zero group, NaN and inf."""
+def test_act_quant_large_input_edge_cases(golden, dt, n):
+    """A multi-wave input (every resident warp loops several times) with an odd row count (a ragged
+    last iteration), the adversarial ue8m0 groups, outliers, a zero group, NaN and inf."""
     rows = 1031
     g = torch.Generator().manual_seed(n)
     x = torch.randn(rows, n, generator=g) * 2
@@ -99,7 +99,6 @@ def test_act_quant_streaming_path_edge_cases(golden, dt, n):
     x[9, 1000] = float("inf")
     x[11, 129] = float("-inf")
     x = x.to(dt)
-    assert x.numel() * x.element_size() >= 8 << 20
     for rs in (False, True):
         y, s = D.act_quant(x.to(DEV), rs)
         yr, sr = O.act_quant_ref(f32_of(x), rs)

@@ -379,10 +379,11 @@ class IndexWorkload(Workload):
             return
         if ev:
             ev[0].record()
-        sc = D.int8_index(q, w, k, ks, causal=self.causal, start=self.start - self.lo)
+        # scores + top-k through the fused entry point (the selection skips causal tails)
+        D.int8_index_topk(q, w, k, ks, topk=self.topk, causal=self.causal, start=self.start - self.lo,
+                          return_scores=True, key_offset=self.lo)
         if ev:
             ev[1].record()
-        D.select_topk(sc.view(self.B * self.M, -1), self.topk, idx_offset=self.lo)
 
     def value(self, ms, world):
         return ms

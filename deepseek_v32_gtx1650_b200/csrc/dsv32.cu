@@ -294,8 +294,42 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
   return DSV32_ERR_UNSUPPORTED;
 }
 
+// One launch of the register top-k: `rows` input rows, each split into nseg segments of seg_len
+// (nseg = 1: whole rows of length n), k selections per segment into out [rows * nseg, k].
+int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
+                    int64_t idx_offset, int k, int32_t* out_idx, float* out_val, int causal_m, int64_t causal_start,
+                    int64_t causal_row0, int seg_len, int nseg, cudaStream_t st) {
+  using namespace dsv32::topk;
+  const int64_t grid = rows * nseg;
+  if (grid > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
+  const unsigned g = static_cast<unsigned>(grid);
+  const long long cs = static_cast<long long>(causal_start), cr0 = static_cast<long long>(causal_row0);
+  if (seg_len <= 256 * 4) {
+    topk_reg_kernel<256, 4><<<g, 256, 0, st>>>(vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx, out_val,
+                                                causal_m, cs, cr0, seg_len, nseg);
+  } else if (seg_len <= 256 * 16) {
+    topk_reg_kernel<256, 16><<<g, 256, 0, st>>>(vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx, out_val,
+                                                 causal_m, cs, cr0, seg_len, nseg);
+  } else {
+    topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx, out_val,
+                                                 causal_m, cs, cr0, seg_len, nseg);
+  }
+  return launch_check("topk kernel launch");
+}
+
+constexpr int kTopkRegMax = 512 * 16;                  // longest row a register pass holds
+constexpr int64_t kTopkTempBytes = int64_t(256) << 20;  // stream-ordered scratch per row batch
+
 // causal_m > 0: row r (= b * causal_m + m) has its scores past key causal_start + m masked to -inf
 // (the indexer's causal rows); those positions are treated as -inf without being read.
+//
+// Rows longer than one register pass are selected in stages: each row is cut into equal segments
+// of at most 8192 positions, every segment keeps its own top-k (a superset of the row's top-k
+// within it), and the segment lists, contiguous and in position order, are merged by the next
+// stage until one pass remains. Candidates keep global positions and their order, so ties resolve
+// exactly as in a single pass. Stage outputs live in stream-ordered scratch (cudaMallocAsync),
+// processed in row batches of at most 256 MB; if the scratch cannot be had, or a segment would be
+// shorter than k, the long-row kernel re-reads the row from L2 instead.
 int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream, int64_t causal_m = 0,
               int64_t causal_start = 0) {
@@ -308,21 +342,77 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   if (int st = device_setup(&dev, &info)) return st;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   using namespace dsv32::topk;
-  const unsigned g = static_cast<unsigned>(rows);
   const int nn = static_cast<int>(n), kk = static_cast<int>(k);
   const int cm = causal_m > 0 && causal_m <= 0x7FFFFFFFLL ? static_cast<int>(causal_m) : 0;
-  if (n <= 256 * 4) {
-    topk_reg_kernel<256, 4><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val,
-                                                 cm, static_cast<long long>(causal_start));
-  } else if (n <= 256 * 16) {
-    topk_reg_kernel<256, 16><<<g, 256, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val,
-                                                 cm, static_cast<long long>(causal_start));
-  } else if (n <= 512 * 16) {
-    topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val,
-                                                 cm, static_cast<long long>(causal_start));
-  } else {
-    topk_gmem_kernel<1024><<<g, 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+  if (n <= kTopkRegMax) {
+    return topk_reg_launch(scores, rows, nn, ld, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, causal_start,
+                           0, nn, 1, st);
   }
+  // Stage plan: segment counts until the candidate list fits one register pass.
+  int plan_nseg[8], plan_seg[8], plan_n[9];
+  int stages = 0;
+  bool staged_ok = true;
+  plan_n[0] = nn;
+  while (plan_n[stages] > kTopkRegMax) {
+    const int cur = plan_n[stages];
+    const int nseg = (cur + kTopkRegMax - 1) / kTopkRegMax;
+    const int seg = ((cur + nseg - 1) / nseg + 3) & ~3;
+    if (stages == 8 || cur - (nseg - 1) * seg < kk || static_cast<int64_t>(nseg) * kk >= cur) {
+      staged_ok = false;
+      break;
+    }
+    plan_nseg[stages] = nseg;
+    plan_seg[stages] = seg;
+    plan_n[stages + 1] = nseg * kk;
+    ++stages;
+  }
+  if (staged_ok) {
+    // Two ping-pong buffers of (idx, val) candidates per row batch.
+    const int64_t per_row = 2 * static_cast<int64_t>(plan_n[1]) * 8;
+    int64_t batch = kTopkTempBytes / per_row;
+    if (batch < 1) batch = 1;
+    if (batch > rows) batch = rows;
+    void* temp = nullptr;
+    if (cudaMallocAsync(&temp, static_cast<size_t>(batch * per_row), st) != cudaSuccess) {
+      cudaGetLastError();
+      temp = nullptr;
+    }
+    if (temp) {
+      int32_t* bi[2] = {static_cast<int32_t*>(temp), static_cast<int32_t*>(temp) + batch * plan_n[1]};
+      float* bv[2] = {reinterpret_cast<float*>(bi[1] + batch * plan_n[1]),
+                      reinterpret_cast<float*>(bi[1] + batch * plan_n[1]) + batch * plan_n[1]};
+      int rc = DSV32_OK;
+      for (int64_t r0 = 0; r0 < rows && rc == DSV32_OK; r0 += batch) {
+        const int64_t rb = (rows - r0 < batch) ? rows - r0 : batch;
+        // stage 0 reads the caller's rows (causal tail skipped), later stages the candidate lists
+        const float* in_v = scores + r0 * ld;
+        const int32_t* in_c = cand_idx ? cand_idx + r0 * cand_ld : nullptr;
+        int64_t in_ld = ld, in_cld = cand_ld, off = idx_offset;
+        int in_cm = cm;
+        int64_t in_cs = causal_start;
+        for (int sidx = 0; sidx < stages && rc == DSV32_OK; ++sidx) {
+          const int b = sidx & 1;
+          rc = topk_reg_launch(in_v, rb, plan_n[sidx], in_ld, in_c, in_cld, off, kk, bi[b], bv[b], in_cm, in_cs, r0,
+                               plan_seg[sidx], plan_nseg[sidx], st);
+          in_v = bv[b];
+          in_c = bi[b];
+          in_ld = in_cld = plan_n[sidx + 1];
+          off = 0;
+          in_cm = 0;
+          in_cs = 0;
+        }
+        if (rc == DSV32_OK)
+          rc = topk_reg_launch(in_v, rb, plan_n[stages], in_ld, in_c, in_cld, off, kk, out_idx + r0 * k,
+                               out_val + r0 * k, in_cm, in_cs, r0, plan_n[stages], 1, st);
+      }
+      const cudaError_t fe = cudaFreeAsync(temp, st);
+      if (rc != DSV32_OK) return rc;
+      if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync");
+      return DSV32_OK;
+    }
+  }
+  topk_gmem_kernel<1024><<<static_cast<unsigned>(rows), 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset,
+                                                                       kk, out_idx, out_val);
   return launch_check("topk kernel launch");
 }
 

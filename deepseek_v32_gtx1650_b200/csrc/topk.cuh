@@ -195,26 +195,36 @@ DSV32_DEV int excl_scan_once(int v, int* buf) {
 // Positions past n hold key 0 (below every real key except the all-ones negative NaN): they never
 // count as above -inf, never reach a histogram while the floor is above -inf, and never equal a
 // threshold >= the -inf key. Only the negative-NaN path (threshold below -inf) checks positions.
+// Causal rows: input row r is causal row r + causal_row0 (a batch of a larger problem).
+// Segmented form: output row r' = blockIdx.x selects from segment r' % nseg (positions
+// [seg0, seg0 + seg_len) of input row r' / nseg); nseg = 1, seg_len = n_total is the plain top-k.
+// Each segment's list is written to out row r' (k entries); the nseg lists of an input row are
+// contiguous, in segment order, so they form that row's candidate list for a merge pass.
 template <int THREADS, int ITEMS>
-__global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restrict__ vals, long long ld, int n,
+__global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restrict__ vals, long long ld, int n_total,
                                                            const int32_t* __restrict__ cand_idx, long long cand_ld,
                                                            long long idx_offset, int k, int32_t* __restrict__ out_idx,
                                                            float* __restrict__ out_val, int causal_m,
-                                                           long long causal_start) {
+                                                           long long causal_start, long long causal_row0,
+                                                           int seg_len, int nseg) {
   constexpr int W = THREADS / 32;
   __shared__ RegShared<THREADS> sh;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int wid = tid >> 5;
-  const long long row = blockIdx.x;
-  const float* v = vals + row * ld;
-  const int valid = row_valid(row, n, causal_m, causal_start);
+  const long long out_row = blockIdx.x;
+  const long long row = out_row / nseg;
+  const int seg0 = static_cast<int>(out_row % nseg) * seg_len;
+  const int n = min(seg_len, n_total - seg0);
+  const float* v = vals + row * ld + seg0;
+  const int valid = max(0, min(n, row_valid(row + causal_row0, n_total, causal_m, causal_start) - seg0));
   const int pos0 = tid * ITEMS;
   for (int i = tid; i < kRegBins; i += THREADS) sh.u.hist[i] = 0;  // first radix pass
   uint32_t key[ITEMS];
   // Each thread owns ITEMS consecutive positions (position order = thread order). Positions in
   // [valid, n) are -inf without a read.
-  if ((ld & 3) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && (ITEMS % 4) == 0 && pos0 + ITEMS <= valid) {
+  if ((ld & 3) == 0 && (seg0 & 3) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && (ITEMS % 4) == 0 &&
+      pos0 + ITEMS <= valid) {
 #pragma unroll
     for (int i = 0; i < ITEMS; i += 4) {
       const float4 f = __ldg(reinterpret_cast<const float4*>(v + pos0 + i));
@@ -397,9 +407,9 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
   const int packed = excl_scan_once<THREADS>((gt << 16) | eq, sh.scan);  // n <= 65535
   const int eq_before = packed & 0xFFFF;
   int o = (packed >> 16) + min(eq_before, krem);
-  const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld : nullptr;
-  int32_t* oi = out_idx + row * k;
-  float* ov = out_val + row * k;
+  const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
+  int32_t* oi = out_idx + out_row * k;
+  float* ov = out_val + out_row * k;
   const bool staged = k <= kStageMax;
   int e = eq_before;
 #pragma unroll
@@ -412,7 +422,7 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
       ++e;
     }
     if (sel) {
-      const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + idx_offset);
+      const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + seg0 + idx_offset);
       const float x = fkey_inv(key[i]);
       if (staged) {
         sh.u.out.idx[o] = id;

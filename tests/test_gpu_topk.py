@@ -119,3 +119,21 @@ def test_index_topk_causal_batched_with_offset(start):
         np.testing.assert_array_equal(npy(idx)[b], ri + 4096)
         np.testing.assert_array_equal(npy(vals)[b], rv)
     assert_no_device_error()
+
+
+def test_index_topk_causal_long_rows_batched():
+    """Rows longer than one register pass are selected in stages, in row batches that bound the
+    scratch; with causal rows the first stage skips each row's masked tail. The result must equal
+    the plain selection over the returned scores (which reads the -inf tail) and the oracle."""
+    B, M, N, topk, start = 1, 5000, 12000, 2048, 6000
+    q, w, k, ks = workloads.index_inputs(B, M, N, seed=21)
+    scores, idx, vals = D.int8_index_topk(q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV), topk=topk, causal=True,
+                                          start=start)
+    pidx, pvals = D.select_topk(scores.view(B * M, N), topk)
+    assert torch.equal(idx.view(B * M, topk), pidx) and torch.equal(vals.view(B * M, topk), pvals)
+    rows = [0, 1, 2047, 2191, 2192, 4095, 4096, 4999]
+    sc = npy(scores)[0][rows]
+    ri, rv = O.topk_ref(sc, topk)
+    np.testing.assert_array_equal(npy(idx)[0][rows], ri)
+    np.testing.assert_array_equal(npy(vals)[0][rows], rv)
+    assert_no_device_error()

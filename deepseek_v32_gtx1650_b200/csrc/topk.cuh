@@ -192,6 +192,24 @@ DSV32_DEV int excl_scan_once(int v, int* buf) {
   return before + incl - v;
 }
 
+// Copies k staged (index, value) pairs from shared memory to a row of the outputs, with 16-byte
+// stores when the row is aligned for them.
+template <int THREADS>
+DSV32_DEV void copy_out_staged(const int32_t* sidx, const float* sval, int32_t* oi, float* ov, int k) {
+  const int tid = threadIdx.x;
+  if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(oi) & 15u) == 0 && (reinterpret_cast<uintptr_t>(ov) & 15u) == 0) {
+    for (int j = tid; j < k / 4; j += THREADS) {
+      reinterpret_cast<int4*>(oi)[j] = reinterpret_cast<const int4*>(sidx)[j];
+      reinterpret_cast<float4*>(ov)[j] = reinterpret_cast<const float4*>(sval)[j];
+    }
+  } else {
+    for (int j = tid; j < k; j += THREADS) {
+      oi[j] = sidx[j];
+      ov[j] = sval[j];
+    }
+  }
+}
+
 // Positions past n hold key 0 (below every real key except the all-ones negative NaN): they never
 // count as above -inf, never reach a histogram while the floor is above -inf, and never equal a
 // threshold >= the -inf key. Only the negative-NaN path (threshold below -inf) checks positions.
@@ -237,6 +255,41 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i)
       key[i] = (pos0 + i < valid) ? fkey(__ldg(v + pos0 + i)) : (pos0 + i < n ? kNegInfKey : 0u);
+  }
+  // 0. A row with at most k visible positions (a causal row that sees <= k keys) selects exactly its
+  //    first k positions: every visible value is above the masked -inf tail, and the tail's ties go
+  //    to the lowest positions. The only exception is a visible negative NaN (below -inf), which
+  //    sends the row down the general path.
+  if (valid <= k) {
+    bool neg_nan = false;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) neg_nan |= (pos0 + i < valid) && key[i] < kNegInfKey;
+    if (!__syncthreads_or(neg_nan)) {  // (the barrier also orders the histogram clear above)
+      const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
+      int32_t* oi = out_idx + out_row * k;
+      float* ov = out_val + out_row * k;
+      const bool staged = k <= kStageMax;
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) {
+        const int pos = pos0 + i;
+        if (pos < k) {
+          const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + seg0 + idx_offset);
+          const float x = fkey_inv(key[i]);
+          if (staged) {
+            sh.u.out.idx[pos] = id;
+            sh.u.out.val[pos] = x;
+          } else {
+            oi[pos] = id;
+            ov[pos] = x;
+          }
+        }
+      }
+      if (staged) {
+        __syncthreads();
+        copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
+      }
+      return;
+    }
   }
   // 1. Row statistics behind one barrier (which also orders the histogram clear before pass 1):
   //    counts above / at the -inf key and the key range of the values above -inf.
@@ -436,18 +489,7 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
   }
   if (staged) {
     __syncthreads();
-    if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(out_idx) & 15u) == 0 &&
-        (reinterpret_cast<uintptr_t>(out_val) & 15u) == 0) {
-      for (int j = tid; j < k / 4; j += THREADS) {
-        reinterpret_cast<int4*>(oi)[j] = reinterpret_cast<const int4*>(sh.u.out.idx)[j];
-        reinterpret_cast<float4*>(ov)[j] = reinterpret_cast<const float4*>(sh.u.out.val)[j];
-      }
-    } else {
-      for (int j = tid; j < k; j += THREADS) {
-        oi[j] = sh.u.out.idx[j];
-        ov[j] = sh.u.out.val[j];
-      }
-    }
+    copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
   }
 }
 

@@ -38,8 +38,9 @@ DSV32_DEV uint32_t fkey(float f) {
 }
 
 DSV32_DEV float fkey_inv(uint32_t k) {
-  const uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
-  return __uint_as_float(u);
+  // top bit set: a positive float with its sign bit raised; clear: a negative float, all bits flipped
+  const uint32_t flip = ~static_cast<uint32_t>(static_cast<int32_t>(k) >> 31) | 0x80000000u;
+  return __uint_as_float(k ^ flip);
 }
 
 // Keys of a row fall into: "above" (> the -inf key: finite, +inf, +NaN), the -inf key, and
@@ -226,6 +227,7 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
                                                            long long causal_start, long long causal_row0,
                                                            int seg_len, int nseg) {
   constexpr int W = THREADS / 32;
+  static_assert(ITEMS <= 32, "per-thread selection masks are 32-bit");
   __shared__ RegShared<THREADS> sh;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -448,43 +450,42 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
     }
     if (!resolved) T = prefix;
   }
-  // 3. Ordered compaction: one scan of (greater, equal) counts gives every thread its output slot.
+  // 3. Ordered compaction: per-thread bit masks of the keys above / at the threshold, one scan of the
+  //    packed counts gives every thread its output slot, and a popcount ranks each selected key.
   const bool check_pos = T < kNegInfKey;  // only a negative-NaN threshold can equal the padding key
-  int gt = 0, eq = 0;
+  uint32_t gmask = 0, emask = 0;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const bool real = !check_pos || pos0 + i < n;
-    gt += (key[i] > T && real) ? 1 : 0;
-    eq += (key[i] == T && real) ? 1 : 0;
+    gmask |= (key[i] > T && real) ? (1u << i) : 0u;
+    emask |= (key[i] == T && real) ? (1u << i) : 0u;
   }
-  const int packed = excl_scan_once<THREADS>((gt << 16) | eq, sh.scan);  // n <= 65535
+  const int eq = __popc(emask);
+  const int packed = excl_scan_once<THREADS>((__popc(gmask) << 16) | eq, sh.scan);  // n <= 65535
   const int eq_before = packed & 0xFFFF;
-  int o = (packed >> 16) + min(eq_before, krem);
+  // keys equal to the threshold are taken in position order: this thread keeps its first `take`
+  int take = max(0, min(eq, krem - eq_before));
+  while (__popc(emask) > take) emask &= ~(0x80000000u >> __clz(emask));  // drop the highest
+  const uint32_t smask = gmask | emask;
+  const int o = (packed >> 16) + min(eq_before, krem);
   const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
   int32_t* oi = out_idx + out_row * k;
   float* ov = out_val + out_row * k;
   const bool staged = k <= kStageMax;
-  int e = eq_before;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
-    const int pos = pos0 + i;
-    const bool real = !check_pos || pos < n;
-    bool sel = key[i] > T && real;
-    if (key[i] == T && real) {
-      sel = e < krem;
-      ++e;
-    }
-    if (sel) {
+    if (smask & (1u << i)) {
+      const int pos = pos0 + i;
+      const int slot = o + __popc(smask & ((1u << i) - 1u));
       const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + seg0 + idx_offset);
       const float x = fkey_inv(key[i]);
       if (staged) {
-        sh.u.out.idx[o] = id;
-        sh.u.out.val[o] = x;
+        sh.u.out.idx[slot] = id;
+        sh.u.out.val[slot] = x;
       } else {
-        oi[o] = id;
-        ov[o] = x;
+        oi[slot] = id;
+        ov[slot] = x;
       }
-      ++o;
     }
   }
   if (staged) {

@@ -132,6 +132,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int64_t slots = (num_groups + GPW - 1) / GPW;
+  pdl_wait();
+  pdl_launch_dependents();
 
   for (int64_t base = warp * UNROLL; base < slots; base += nwarps * UNROLL) {
     // All UNROLL 16-byte loads of the lane are issued before any is used; the raw vectors stay

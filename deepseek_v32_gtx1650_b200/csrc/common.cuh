@@ -43,6 +43,16 @@ DSV32_DEV uint32_t lane_id() {
   return r;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the library is launched with programmatic stream serialization: it may start
+// while the previous kernel on the stream is still finishing. pdl_wait() blocks until that kernel
+// has completed and its memory is visible, so each kernel calls it before its first global memory
+// access (only shared-memory / TMEM set-up runs before it). pdl_launch_dependents() then lets the
+// next kernel's CTAs be scheduled early; they wait the same way. Without the launch attribute
+// both are no-ops.
+DSV32_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DSV32_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 DSV32_DEV void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

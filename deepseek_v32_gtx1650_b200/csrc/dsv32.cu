@@ -138,6 +138,27 @@ int launch_check(const char* what) {
   return DSV32_OK;
 }
 
+// Launches a kernel with programmatic stream serialization (see pdl_wait in common.cuh): it may
+// be scheduled while the previous kernel on the stream finishes, and waits for it before touching
+// global memory. Arguments are converted to the kernel's parameter types.
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st, const char* what,
+           Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return launch_check(what);
+}
+
 struct GemmPlan {
   int BN;
   int64_t tiles, units;
@@ -199,22 +220,20 @@ int gemm_launch(const GemmPlan& plan, const int8_t* a, const float* a_s, const i
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
   const uint32_t ok = partials ? kOutF32 : static_cast<uint32_t>(c_dtype);
   const int cap = static_cast<int>(plan.ws_tiles_cap), sr = plan.slot_rows;
+  const unsigned g = static_cast<unsigned>(plan.grid);
+  const char* what = "int8_gemm_kernel launch";
   if (plan.BN == 256) {
     if (partials)
-      int8_gemm_kernel<256, true><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                 ki, partials, ws, cap, sr);
-    else
-      int8_gemm_kernel<256, false><<<plan.grid, kThreads, Smem<256>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                  ki, nullptr, ws, cap, sr);
-  } else {
-    if (partials)
-      int8_gemm_kernel<128, true><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                 ki, partials, ws, cap, sr);
-    else
-      int8_gemm_kernel<128, false><<<plan.grid, kThreads, Smem<128>::kAlloc, st>>>(tmA, tmB, a_s, b_s, c, ok, mi, ni,
-                                                                                  ki, nullptr, ws, cap, sr);
+      return launch(int8_gemm_kernel<256, true>, g, kThreads, Smem<256>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok,
+                    mi, ni, ki, partials, ws, cap, sr);
+    return launch(int8_gemm_kernel<256, false>, g, kThreads, Smem<256>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok, mi,
+                  ni, ki, static_cast<int32_t*>(nullptr), ws, cap, sr);
   }
-  return launch_check("int8_gemm_kernel launch");
+  if (partials)
+    return launch(int8_gemm_kernel<128, true>, g, kThreads, Smem<128>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok, mi,
+                  ni, ki, partials, ws, cap, sr);
+  return launch(int8_gemm_kernel<128, false>, g, kThreads, Smem<128>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok, mi,
+                ni, ki, static_cast<int32_t*>(nullptr), ws, cap, sr);
 }
 
 int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype, int64_t m,
@@ -253,10 +272,10 @@ int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w,
   const int64_t units = batch * nqb * chunks;
   if (units > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
   const int64_t grid = units < num_sms ? units : num_sms;  // persistent: one CTA per SM
-  int8_index_kernel<H, D><<<static_cast<unsigned>(grid), kThreads, C::kAlloc, st>>>(
-      tmQ, tmK, w, k_s, out, static_cast<int>(m), static_cast<int>(n), causal, static_cast<long long>(start),
-      static_cast<int>(tpc), static_cast<int>(chunks), static_cast<int>(units));
-  return launch_check("int8_index_kernel launch");
+  return launch(int8_index_kernel<H, D>, static_cast<unsigned>(grid), kThreads, C::kAlloc, st,
+                "int8_index_kernel launch", tmQ, tmK, w, k_s, out, static_cast<int>(m), static_cast<int>(n), causal,
+                static_cast<long long>(start), static_cast<int>(tpc), static_cast<int>(chunks),
+                static_cast<int>(units));
 }
 
 int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
@@ -304,17 +323,15 @@ int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const in
   if (grid > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
   const unsigned g = static_cast<unsigned>(grid);
   const long long cs = static_cast<long long>(causal_start), cr0 = static_cast<long long>(causal_row0);
-  if (seg_len <= 256 * 4) {
-    topk_reg_kernel<256, 4><<<g, 256, 0, st>>>(vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx, out_val,
-                                                causal_m, cs, cr0, seg_len, nseg);
-  } else if (seg_len <= 256 * 16) {
-    topk_reg_kernel<256, 16><<<g, 256, 0, st>>>(vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx, out_val,
-                                                 causal_m, cs, cr0, seg_len, nseg);
-  } else {
-    topk_reg_kernel<512, 16><<<g, 512, 0, st>>>(vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx, out_val,
-                                                 causal_m, cs, cr0, seg_len, nseg);
-  }
-  return launch_check("topk kernel launch");
+  const char* what = "topk kernel launch";
+  if (seg_len <= 256 * 4)
+    return launch(topk_reg_kernel<256, 4>, g, 256, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx,
+                  out_val, causal_m, cs, cr0, seg_len, nseg);
+  if (seg_len <= 256 * 16)
+    return launch(topk_reg_kernel<256, 16>, g, 256, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k,
+                  out_idx, out_val, causal_m, cs, cr0, seg_len, nseg);
+  return launch(topk_reg_kernel<512, 16>, g, 512, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx,
+                out_val, causal_m, cs, cr0, seg_len, nseg);
 }
 
 constexpr int kTopkRegMax = 512 * 16;                  // longest row a register pass holds
@@ -411,9 +428,8 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
       return DSV32_OK;
     }
   }
-  topk_gmem_kernel<1024><<<static_cast<unsigned>(rows), 1024, 0, st>>>(scores, ld, nn, cand_idx, cand_ld, idx_offset,
-                                                                       kk, out_idx, out_val);
-  return launch_check("topk kernel launch");
+  return launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rows), 1024, 0, st, "topk kernel launch", scores, ld, nn,
+                cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
 }
 
 }  // namespace
@@ -460,17 +476,16 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
   // One wave of resident CTAs, each looping over its share: no tail wave.
   const int64_t cap = static_cast<int64_t>(info->num_sms) * info->aq_blocks_per_sm[x_dtype];
   if (blocks > cap) blocks = cap;
-  if (x_dtype == DSV32_F32) {
-    act_quant_kernel<float, kAqUnrollF32><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
-        static_cast<const float*>(x), y, s, groups, round_scale);
-  } else if (x_dtype == DSV32_BF16) {
-    act_quant_kernel<__nv_bfloat16, kAqUnroll16><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), y, s, groups, round_scale);
-  } else {
-    act_quant_kernel<__half, kAqUnroll16><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
-        static_cast<const __half*>(x), y, s, groups, round_scale);
-  }
-  return launch_check("act_quant_kernel launch");
+  const unsigned g = static_cast<unsigned>(blocks);
+  const char* what = "act_quant_kernel launch";
+  if (x_dtype == DSV32_F32)
+    return launch(act_quant_kernel<float, kAqUnrollF32>, g, threads, 0, st, what, static_cast<const float*>(x), y, s,
+                  groups, round_scale);
+  if (x_dtype == DSV32_BF16)
+    return launch(act_quant_kernel<__nv_bfloat16, kAqUnroll16>, g, threads, 0, st, what,
+                  static_cast<const __nv_bfloat16*>(x), y, s, groups, round_scale);
+  return launch(act_quant_kernel<__half, kAqUnroll16>, g, threads, 0, st, what, static_cast<const __half*>(x), y, s,
+                groups, round_scale);
 }
 
 int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,

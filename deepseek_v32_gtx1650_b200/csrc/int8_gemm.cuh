@@ -236,6 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // no global memory access before this point
+  pdl_launch_dependents();
 
   if (warp >= kEpiWarps) {
     regs_dec<kCtlRegs>();

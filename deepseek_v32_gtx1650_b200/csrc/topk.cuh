@@ -239,6 +239,8 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
   const float* v = vals + row * ld + seg0;
   const int valid = max(0, min(n, row_valid(row + causal_row0, n_total, causal_m, causal_start) - seg0));
   const int pos0 = tid * ITEMS;
+  pdl_wait();
+  pdl_launch_dependents();
   for (int i = tid; i < kRegBins; i += THREADS) sh.u.hist[i] = 0;  // first radix pass
   uint32_t key[ITEMS];
   // Each thread owns ITEMS consecutive positions (position order = thread order). Positions in
@@ -504,6 +506,8 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
   int parity = 0;
   const long long row = blockIdx.x;
   const float* v = vals + row * ld;
+  pdl_wait();
+  pdl_launch_dependents();
   int n_above = 0, n_ninf = 0;
   for (int i = threadIdx.x; i < n; i += THREADS) {
     const uint32_t kk = fkey(__ldg(v + i));

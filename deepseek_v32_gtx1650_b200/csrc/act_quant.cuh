@@ -16,7 +16,7 @@
 // are in flight per lane (HBM latency hiding).
 //
 // Per value the work stays on the FP32 pipe: amax with a NaN-propagating max, the rounding as a
-// fused multiply-add with 1.5 * 2^23 whose result bits carry the int8 (aq_quant_bits), and byte
+// fused multiply-add with 1.5 * 2^23 whose result bits carry the int8 (aq_quant_lane), and byte
 // permutes to pack four results; no float -> int conversion instruction. Values within 2^-14 of a
 // rounding tie (about 1 in 8000) are recomputed with the IEEE division.
 #pragma once
@@ -72,7 +72,7 @@ DSV32_DEV float max_nan(float a, float b) {
 }
 
 // Reciprocal with at most 1 ulp of error (the PTX approximate reciprocal): enough for
-// aq_quant_bits, whose exactness argument allows 2^-23 relative error in r.
+// aq_quant_lane, whose exactness argument allows 2^-23 relative error in r.
 DSV32_DEV float rcp_1ulp(float x) {
   float r;
   asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
@@ -94,6 +94,14 @@ DSV32_DEV float aq_scale(float amax, bool round_scale) {
   return s;
 }
 
+constexpr float kAqTieBound = 0.5f - 6.103515625e-05f;  // 1/2 - 2^-14
+
+// fp32 bits of rint(fl(x / s)) + 1.5 * 2^23 through the IEEE division; NaN -> 0.
+DSV32_DEV float aq_exact_bits(float x, float s) {
+  const float v = rintf(__fdiv_rn(x, s));
+  return (v == v) ? v + 12582912.0f : 12582912.0f;
+}
+
 // round_half_even(x / s) for |x| <= amax, s = amax-derived scale (|x / s| <= 127 + tiny), returned as
 // the fp32 bits of q + 1.5 * 2^23, whose low byte is q as a two's-complement int8. No conversion
 // instruction: fma(x, r, 1.5 * 2^23) rounds the exact product x * r once, to the nearest integer
@@ -101,19 +109,29 @@ DSV32_DEV float aq_scale(float amax, bool round_scale) {
 // of 1/s, x * r is within 2^-16 + 2^-18 of fl(x / s) for |q| < 128 (2^-23 relative for r, half an
 // ulp for the quotient), so rint(x * r) == rint(fl(x / s)) unless x * r lies within 2^-14 of a half
 // integer; those (about 1 in 8000) and NaN products take the IEEE division. NaN converts to 0.
-DSV32_DEV uint32_t aq_quant_bits(float x, float s, float r) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  float big = fmaf(x, r, kMagic);
-  const float n = big - kMagic;    // rint(x * r), exact
-  const float t = fmaf(x, r, -n);  // x * r - rint(x * r)
-  if (!(fabsf(t) <= 0.5f - 6.103515625e-05f)) {  // near a tie, or NaN
-    const float v = rintf(__fdiv_rn(x, s));
-    big = (v == v) ? v + kMagic : kMagic;
+// Applied to the EPL values of one lane with a single (rarely taken) branch: the fast results and one
+// "near a tie / NaN" flag per lane, then the exact path for the flagged values only.
+template <int EPL>
+DSV32_DEV void aq_quant_lane(const float (&f)[EPL], float s, float r, uint32_t (&bits)[EPL]) {
+  constexpr float kMagic = 12582912.0f;
+  bool slow = false;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float big = fmaf(f[e], r, kMagic);
+    const float t = fmaf(f[e], r, -(big - kMagic));
+    slow |= !(fabsf(t) <= kAqTieBound);
+    bits[e] = __float_as_uint(big);
   }
-  return __float_as_uint(big);
+  if (slow) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float t = fmaf(f[e], r, -(__uint_as_float(bits[e]) - kMagic));
+      if (!(fabsf(t) <= kAqTieBound)) bits[e] = __float_as_uint(aq_exact_bits(f[e], s));
+    }
+  }
 }
 
-// Low bytes of four aq_quant_bits results, in order, as one 32-bit word.
+// Low bytes of four aq_quant_lane results, in order, as one 32-bit word.
 DSV32_DEV uint32_t aq_pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
@@ -166,16 +184,13 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
       const float sc = aq_scale(amax, round_scale != 0);
       const float rc = rcp_1ulp(sc);
       if (valid) {
+        uint32_t qb[EPL];
+        aq_quant_lane<EPL>(f, sc, rc, qb);
         if constexpr (EPL == 4) {
-          const uint32_t w0 = aq_pack4(aq_quant_bits(f[0], sc, rc), aq_quant_bits(f[1], sc, rc),
-                                       aq_quant_bits(f[2], sc, rc), aq_quant_bits(f[3], sc, rc));
-          __stcs(reinterpret_cast<unsigned int*>(y + g * 128) + sl, w0);
+          __stcs(reinterpret_cast<unsigned int*>(y + g * 128) + sl, aq_pack4(qb[0], qb[1], qb[2], qb[3]));
         } else {
-          const uint32_t w0 = aq_pack4(aq_quant_bits(f[0], sc, rc), aq_quant_bits(f[1], sc, rc),
-                                       aq_quant_bits(f[2], sc, rc), aq_quant_bits(f[3], sc, rc));
-          const uint32_t w1 = aq_pack4(aq_quant_bits(f[4], sc, rc), aq_quant_bits(f[5], sc, rc),
-                                       aq_quant_bits(f[6], sc, rc), aq_quant_bits(f[7], sc, rc));
-          __stcs(reinterpret_cast<uint2*>(y + g * 128) + sl, make_uint2(w0, w1));
+          __stcs(reinterpret_cast<uint2*>(y + g * 128) + sl,
+                 make_uint2(aq_pack4(qb[0], qb[1], qb[2], qb[3]), aq_pack4(qb[4], qb[5], qb[6], qb[7])));
         }
         if (sl == 0) s[g] = sc;
       }

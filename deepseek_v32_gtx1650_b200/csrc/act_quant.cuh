@@ -24,24 +24,6 @@
 
 namespace dsv32 {
 
-template <typename T>
-struct AqTraits;
-template <>
-struct AqTraits<float> {
-  static constexpr int kLanesPerGroup = 32;  // 32 lanes x 4 fp32
-  static constexpr int kElemsPerLane = 4;
-};
-template <>
-struct AqTraits<__nv_bfloat16> {
-  static constexpr int kLanesPerGroup = 16;  // 16 lanes x 8 bf16
-  static constexpr int kElemsPerLane = 8;
-};
-template <>
-struct AqTraits<__half> {
-  static constexpr int kLanesPerGroup = 16;
-  static constexpr int kElemsPerLane = 8;
-};
-
 DSV32_DEV void to_f32(const float4& v, float (&f)[4]) {
   f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
 }
@@ -111,16 +93,20 @@ DSV32_DEV float aq_exact_bits(float x, float s) {
 // integer; those (about 1 in 8000) and NaN products take the IEEE division. NaN converts to 0.
 // Applied to the EPL values of one lane with a single (rarely taken) branch: the fast results and one
 // "near a tie / NaN" flag per lane, then the exact path for the flagged values only.
+// Pairs of values use the packed f32x2 FMA: big = x*r + M, -n = big*(-1) + M (exact), t = x*r - n.
 template <int EPL>
 DSV32_DEV void aq_quant_lane(const float (&f)[EPL], float s, float r, uint32_t (&bits)[EPL]) {
   constexpr float kMagic = 12582912.0f;
+  const float2 r2 = make_float2(r, r), m2 = make_float2(kMagic, kMagic), neg1 = make_float2(-1.f, -1.f);
   bool slow = false;
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    const float big = fmaf(f[e], r, kMagic);
-    const float t = fmaf(f[e], r, -(big - kMagic));
-    slow |= !(fabsf(t) <= kAqTieBound);
-    bits[e] = __float_as_uint(big);
+  for (int e = 0; e < EPL; e += 2) {
+    const float2 x2 = make_float2(f[e], f[e + 1]);
+    const float2 big = __ffma2_rn(x2, r2, m2);
+    const float2 t = __ffma2_rn(x2, r2, __ffma2_rn(big, neg1, m2));
+    slow |= !(fabsf(t.x) <= kAqTieBound) || !(fabsf(t.y) <= kAqTieBound);
+    bits[e] = __float_as_uint(big.x);
+    bits[e + 1] = __float_as_uint(big.y);
   }
   if (slow) {
 #pragma unroll
@@ -136,14 +122,17 @@ DSV32_DEV uint32_t aq_pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-template <typename T, int UNROLL>
+// EPL values of a group per lane (LPG = 128 / EPL lanes per group, 32 / LPG groups per warp slot),
+// read as EPL * sizeof(T) / 16 consecutive 16-byte vectors; UNROLL group slots per iteration.
+template <typename T, int EPL, int UNROLL>
 __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
                                                         float* __restrict__ s, int64_t num_groups,
                                                         int round_scale) {
-  using Tr = AqTraits<T>;
-  constexpr int LPG = Tr::kLanesPerGroup;
-  constexpr int EPL = Tr::kElemsPerLane;
+  constexpr int LPG = 128 / EPL;
   constexpr int GPW = 32 / LPG;  // groups per warp-slot
+  constexpr int NV = EPL * static_cast<int>(sizeof(T)) / 16;  // 16-byte vectors per lane
+  constexpr int FPV = 16 / static_cast<int>(sizeof(T));        // values per vector
+  static_assert(NV >= 1 && LPG >= 1 && LPG <= 32 && EPL % 4 == 0, "unsupported lane split");
   const int lane = threadIdx.x & 31;
   const int sub = lane / LPG;     // which group of the slot this lane works on
   const int sl = lane % LPG;      // lane within the group
@@ -154,26 +143,31 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
   pdl_launch_dependents();
 
   for (int64_t base = warp * UNROLL; base < slots; base += nwarps * UNROLL) {
-    // All UNROLL 16-byte loads of the lane are issued before any is used; the raw vectors stay
-    // packed in registers until their group is processed.
-    uint4 raw[UNROLL];
+    // All loads of the lane are issued before any is used; the raw vectors stay packed in
+    // registers until their group is processed.
+    uint4 raw[UNROLL][NV];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int64_t g = (base + u) * GPW + sub;
-      raw[u] = ((base + u) < slots && g < num_groups) ? __ldcs(reinterpret_cast<const uint4*>(x + g * 128) + sl)
-                                                      : make_uint4(0u, 0u, 0u, 0u);
+      const bool valid = (base + u) < slots && g < num_groups;
+      const uint4* src = reinterpret_cast<const uint4*>(x + g * 128 + sl * EPL);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) raw[u][j] = valid ? __ldcs(src + j) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int64_t g = (base + u) * GPW + sub;
       const bool valid = (base + u) < slots && g < num_groups;
       float f[EPL];
-      if constexpr (sizeof(T) == 4) {
-        to_f32(make_float4(__uint_as_float(raw[u].x), __uint_as_float(raw[u].y), __uint_as_float(raw[u].z),
-                           __uint_as_float(raw[u].w)),
-               reinterpret_cast<float(&)[4]>(f));
-      } else {
-        to_f32(raw[u], reinterpret_cast<float(&)[8]>(f), static_cast<T*>(nullptr));
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        if constexpr (sizeof(T) == 4) {
+          to_f32(make_float4(__uint_as_float(raw[u][j].x), __uint_as_float(raw[u][j].y),
+                             __uint_as_float(raw[u][j].z), __uint_as_float(raw[u][j].w)),
+                 *reinterpret_cast<float(*)[4]>(f + j * FPV));
+        } else {
+          to_f32(raw[u][j], *reinterpret_cast<float(*)[8]>(f + j * FPV), static_cast<T*>(nullptr));
+        }
       }
       float a = 0.f;
 #pragma unroll
@@ -186,11 +180,20 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
       if (valid) {
         uint32_t qb[EPL];
         aq_quant_lane<EPL>(f, sc, rc, qb);
+        int8_t* dst = y + g * 128 + sl * EPL;
         if constexpr (EPL == 4) {
-          __stcs(reinterpret_cast<unsigned int*>(y + g * 128) + sl, aq_pack4(qb[0], qb[1], qb[2], qb[3]));
+          __stcs(reinterpret_cast<unsigned int*>(dst), aq_pack4(qb[0], qb[1], qb[2], qb[3]));
+        } else if constexpr (EPL == 8) {
+          __stcs(reinterpret_cast<uint2*>(dst), make_uint2(aq_pack4(qb[0], qb[1], qb[2], qb[3]),
+                                                           aq_pack4(qb[4], qb[5], qb[6], qb[7])));
         } else {
-          __stcs(reinterpret_cast<uint2*>(y + g * 128) + sl,
-                 make_uint2(aq_pack4(qb[0], qb[1], qb[2], qb[3]), aq_pack4(qb[4], qb[5], qb[6], qb[7])));
+#pragma unroll
+          for (int j = 0; j < EPL / 16; ++j)
+            __stcs(reinterpret_cast<uint4*>(dst) + j,
+                   make_uint4(aq_pack4(qb[16 * j + 0], qb[16 * j + 1], qb[16 * j + 2], qb[16 * j + 3]),
+                              aq_pack4(qb[16 * j + 4], qb[16 * j + 5], qb[16 * j + 6], qb[16 * j + 7]),
+                              aq_pack4(qb[16 * j + 8], qb[16 * j + 9], qb[16 * j + 10], qb[16 * j + 11]),
+                              aq_pack4(qb[16 * j + 12], qb[16 * j + 13], qb[16 * j + 14], qb[16 * j + 15])));
         }
         if (sl == 0) s[g] = sc;
       }

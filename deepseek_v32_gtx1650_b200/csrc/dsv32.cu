@@ -19,8 +19,11 @@
 
 namespace {
 
-// act_quant: 16-byte loads in flight per lane per iteration, by input width (fp32, 16-bit).
-constexpr int kAqUnrollF32 = 4;
+// act_quant lane split and loads in flight, by input width (fp32, 16-bit): values of a group per
+// lane, and group slots per lane per iteration.
+constexpr int kAqEplF32 = 8;
+constexpr int kAqUnrollF32 = 2;
+constexpr int kAqEpl16 = 8;
 constexpr int kAqUnroll16 = 4;
 
 thread_local std::string t_last_error;
@@ -89,12 +92,15 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64>, index::Cfg<16, 64>::kAlloc));
       {
         int nb = 0;
-        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<float, kAqUnrollF32>, 256, 0));
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &nb, act_quant_kernel<float, kAqEplF32, kAqUnrollF32>, 256, 0));
         d.aq_blocks_per_sm[DSV32_F32] = nb > 0 ? nb : 1;
         DSV32_CUDA_TRY(
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__nv_bfloat16, kAqUnroll16>, 256, 0));
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__nv_bfloat16, kAqEpl16, kAqUnroll16>,
+                                                          256, 0));
         d.aq_blocks_per_sm[DSV32_BF16] = nb > 0 ? nb : 1;
-        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__half, kAqUnroll16>, 256, 0));
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &nb, act_quant_kernel<__half, kAqEpl16, kAqUnroll16>, 256, 0));
         d.aq_blocks_per_sm[DSV32_F16] = nb > 0 ? nb : 1;
       }
       if (!g_encode) {
@@ -469,7 +475,7 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
   using namespace dsv32;
   const int unroll = (x_dtype == DSV32_F32) ? kAqUnrollF32 : kAqUnroll16;
   const int threads = 256;
-  const int gpw = (x_dtype == DSV32_F32) ? 1 : 2;
+  const int gpw = 32 / (128 / ((x_dtype == DSV32_F32) ? kAqEplF32 : kAqEpl16));  // groups per warp slot
   const int64_t slots = (groups + gpw - 1) / gpw;
   const int64_t warps_needed = (slots + unroll - 1) / unroll;
   int64_t blocks = (warps_needed + (threads / 32) - 1) / (threads / 32);
@@ -479,13 +485,13 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
   const unsigned g = static_cast<unsigned>(blocks);
   const char* what = "act_quant_kernel launch";
   if (x_dtype == DSV32_F32)
-    return launch(act_quant_kernel<float, kAqUnrollF32>, g, threads, 0, st, what, static_cast<const float*>(x), y, s,
-                  groups, round_scale);
+    return launch(act_quant_kernel<float, kAqEplF32, kAqUnrollF32>, g, threads, 0, st, what,
+                  static_cast<const float*>(x), y, s, groups, round_scale);
   if (x_dtype == DSV32_BF16)
-    return launch(act_quant_kernel<__nv_bfloat16, kAqUnroll16>, g, threads, 0, st, what,
+    return launch(act_quant_kernel<__nv_bfloat16, kAqEpl16, kAqUnroll16>, g, threads, 0, st, what,
                   static_cast<const __nv_bfloat16*>(x), y, s, groups, round_scale);
-  return launch(act_quant_kernel<__half, kAqUnroll16>, g, threads, 0, st, what, static_cast<const __half*>(x), y, s,
-                groups, round_scale);
+  return launch(act_quant_kernel<__half, kAqEpl16, kAqUnroll16>, g, threads, 0, st, what,
+                static_cast<const __half*>(x), y, s, groups, round_scale);
 }
 
 int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,

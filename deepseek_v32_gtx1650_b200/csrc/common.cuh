@@ -260,6 +260,16 @@ DSV32_DEV float relu_i32_x2m22(uint32_t bits) {
   return r;
 }
 
+// Width-generic forms of the pipelined TMEM reads (16 or 32 columns).
+template <int W>
+DSV32_DEV void tmem_ld_async(uint32_t taddr, uint32_t (&r)[W]) {
+  if constexpr (W == 32) tmem_ld32_async(taddr, r); else tmem_ld16_async(taddr, r);
+}
+template <int W>
+DSV32_DEV void tmem_wait_ld(uint32_t (&r)[W]) {
+  if constexpr (W == 32) tmem_wait_ld32(r); else tmem_wait_ld16(r);
+}
+
 // Register re-balancing between warpgroups (all 4 warps of a warpgroup execute it).
 template <uint32_t N>
 DSV32_DEV void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }

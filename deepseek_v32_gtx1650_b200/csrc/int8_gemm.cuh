@@ -8,9 +8,10 @@
 // the K-major operand form tcgen05 reads; a_s [M, K/128], b_s [N/128, K/128] fp32.
 //
 // Roles (one CTA per SM, 384 threads):
-//   warp 8      TMA producer: 128x128 A and BNx128 B tiles (SWIZZLE_128B) into a 4-stage ring.
+//   warp 8      TMA producer: 128x128 A and BNx128 B tiles (SWIZZLE_128B) into a 192 KB ring
+//               (4 stages for BN = 256, 6 for BN = 128).
 //   warp 9      MMA issuer: per 128-K block, 4 x tcgen05.mma.kind::i8 (K = 32 each) into one of
-//               two TMEM int32 accumulators (BN columns each), committed to the epilogue.
+//               512 / BN TMEM int32 accumulators (BN columns each), committed to the epilogue.
 //   warps 0-7   promotion epilogue: for every K block, tcgen05.ld the int32 partial, convert it
 //               to fp32 (exact: |partial| <= 128*127*127 < 2^24), multiply by a_s*b_s and
 //               accumulate in fp32 registers (packed f32x2 FMA), then release the TMEM buffer.
@@ -36,7 +37,6 @@ namespace gemm {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;
-constexpr int kStages = 4;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 idle
 // Launch: 384 threads x 168 registers = 64512. setmaxnreg moves them to the epilogue:
@@ -54,13 +54,15 @@ constexpr int kMmaWarp = kEpiWarps + 1;
 
 template <int BN>
 struct Smem {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;  // operand ring depth (192 KB either way)
+  static constexpr int kTB = 512 / BN;                 // TMEM accumulator buffers (all 512 columns)
   static constexpr int kA = kBM * kBK;          // bytes per A stage
   static constexpr int kB = BN * kBK;           // bytes per B stage
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kA;
   static constexpr int kOffBar = kOffB + kStages * kB;
-  // full[kStages], empty[kStages], tfull[2], tempty[2], mma_done
-  static constexpr int kNumBars = 2 * kStages + 5;
+  // full[kStages], empty[kStages], tfull[kTB], tempty[kTB], mma_done
+  static constexpr int kNumBars = 2 * kStages + 2 * kTB + 1;
   static constexpr int kOffTmem = kOffBar + 8 * kNumBars;
   static constexpr int kOffAbort = kOffTmem + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -139,11 +141,12 @@ DSV32_DEV void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-// acc[0..7] += float(partial) * sc for 16 columns (8 float2 pairs); the int32 -> fp32 conversion
+// acc[0..W/2) += float(partial) * sc for W columns (float2 pairs); the int32 -> fp32 conversion
 // is exact for these magnitudes.
-DSV32_DEV void promote16(const uint32_t (&r)[16], float2* acc, float2 sc2) {
+template <int W>
+DSV32_DEV void promote(const uint32_t (&r)[W], float2* acc, float2 sc2) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < W / 2; ++j) {
     const float2 v = make_float2(static_cast<float>(static_cast<int32_t>(r[2 * j])),
                                  static_cast<float>(static_cast<int32_t>(r[2 * j + 1])));
     acc[j] = __ffma2_rn(v, sc2, acc[j]);
@@ -201,10 +204,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sB = base + L::kOffB;
   const uint32_t bar0 = base + L::kOffBar;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  constexpr int kStages = L::kStages;
+  constexpr int kTB = L::kTB;
   auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
   auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * kStages + b); };
-  auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * kStages + 2 + b); };
-  const uint32_t mma_done_bar = bar0 + 8u * (2 * kStages + 4);
+  auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * kStages + kTB + b); };
+  const uint32_t mma_done_bar = bar0 + 8u * (2 * kStages + 2 * kTB);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffTmem);
 
@@ -223,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTB; ++b) {
       mbar_init(tfull_bar(b), 1);
       mbar_init(tempty_bar(b), kEpiWarps);
     }
@@ -231,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) tmem_alloc(smem_u32(tmem_slot), 2 * BN);
+  if (warp == kMmaWarp) tmem_alloc(smem_u32(tmem_slot), kTB * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -292,8 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool first;
       while (ok && it.next(tile, kb0, kb1, first)) {
         for (int kb = kb0; kb < kb1; ++kb, ++u) {
-          const uint32_t buf = u & 1u;
-          if (!mbar_wait(tempty_bar(buf), (u >> 1) & 1u, abort_flag, (KID_GEMM << 16) | 2) ||
+          const uint32_t buf = u % kTB;
+          if (!mbar_wait(tempty_bar(buf), (u / kTB) & 1u, abort_flag, (KID_GEMM << 16) | 2) ||
               !mbar_wait(full_bar(stage), phase, abort_flag, (KID_GEMM << 16) | 3)) {
             ok = false;
             break;
@@ -332,8 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Both accumulators start free.
     __syncwarp();
     if (lane == 0) {
-      mbar_arrive(tempty_bar(0));
-      mbar_arrive(tempty_bar(1));
+      for (int b = 0; b < kTB; ++b) mbar_arrive(tempty_bar(b));
     }
     uint32_t u = 0;
     SegIter it(sch);
@@ -355,28 +359,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       float sa_next = row_ok ? __ldg(as_row + kb0) : 0.f;
       float sb_next = cols_ok ? __ldg(bs_row + kb0) : 0.f;
       for (int kb = kb0; kb < kb1; ++kb, ++u) {
-        const uint32_t buf = u & 1u;
+        const uint32_t buf = u % kTB;
         const float sc = sa_next * sb_next;
         if (kb + 1 < kb1) {  // prefetch the next block's scales
           sa_next = row_ok ? __ldg(as_row + kb + 1) : 0.f;
           sb_next = cols_ok ? __ldg(bs_row + kb + 1) : 0.f;
         }
         const float2 sc2 = make_float2(sc, sc);
-        if (!mbar_wait_warp(tfull_bar(buf), (u >> 1) & 1u, abort_flag, (KID_GEMM << 16) | 4)) {
+        if (!mbar_wait_warp(tfull_bar(buf), (u / kTB) & 1u, abort_flag, (KID_GEMM << 16) | 4)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t tb = t_lane + buf * BN;
-        constexpr int kCW = 16;  // columns per TMEM read
+        // TMEM reads are software-pipelined one chunk ahead; 32-column chunks when the 64
+        // accumulators of a BN=128 tile leave room for two of them, else 16 columns.
+        constexpr int kCW = (kCols <= 64) ? 32 : 16;
         uint32_t ra[kCW], rb[kCW];
-        tmem_ld16_async(tb, ra);
-        tmem_wait_ld16(ra);
+        tmem_ld_async<kCW>(tb, ra);
+        tmem_wait_ld<kCW>(ra);
 #pragma unroll
         for (int c = 0; c < kCols / kCW; ++c) {
           uint32_t(&cur)[kCW] = (c & 1) ? rb : ra;
           uint32_t(&nxt)[kCW] = (c & 1) ? ra : rb;
-          if (c + 1 < kCols / kCW) tmem_ld16_async(tb + (c + 1) * kCW, nxt);  // in flight during promote
+          if (c + 1 < kCols / kCW) tmem_ld_async<kCW>(tb + (c + 1) * kCW, nxt);  // in flight during promote
           if constexpr (kPartials) {
             if (row_ok && cols_ok) {
               int32_t* p = partials + (static_cast<int64_t>(kb) * M + row) * N + col0 + c * kCW;
@@ -384,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < kCW; ++j) p[j] = static_cast<int32_t>(cur[j]);
             }
           }
-          promote16(cur, acc + c * (kCW / 2), sc2);
-          if (c + 1 < kCols / kCW) tmem_wait_ld16(nxt);
+          promote<kCW>(cur, acc + c * (kCW / 2), sc2);
+          if (c + 1 < kCols / kCW) tmem_wait_ld<kCW>(nxt);
         }
         tc_fence_before();
         __syncwarp();
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (warp == kMmaWarp) {
     __syncwarp();
-    tmem_dealloc(tmem_base, 2 * BN);
+    tmem_dealloc(tmem_base, kTB * BN);
   }
 }
 

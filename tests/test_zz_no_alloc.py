@@ -48,8 +48,9 @@ def test_noalloc_matches_regular_entry_point_on_two_calls(M, N, K, dt):
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    """m = 64 over n = 7168 has fewer tiles than SMs and needs about 19 MiB of scratch."""
-    M, N, K = 64, 7168, 2048
+    """m = 128 over n = 7168 has fewer tiles than SMs (56 tiles of 128x128) and needs about 19 MiB of
+    scratch for its split-K partials."""
+    M, N, K = 128, 7168, 2048
     a, a_s, b, b_s = (t.to(DEV) for t in workloads.gemm_inputs_uniform(M, N, K, seed=1))
     c = torch.zeros(M, N, device=DEV)
     st = _noalloc(a, a_s, b, b_s, c)

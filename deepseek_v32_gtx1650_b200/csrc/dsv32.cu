@@ -16,6 +16,7 @@
 #include "int8_gemm.cuh"
 #include "int8_index.cuh"
 #include "topk.cuh"
+#include "producers.cuh"
 
 namespace {
 
@@ -569,6 +570,57 @@ int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, cons
   if (int st = index_impl(q, w, k, k_s, scores, batch, m, n, heads, dim, causal, start, stream)) return st;
   return topk_impl(scores, batch * m, n, n, nullptr, 0, key_offset, topk, out_idx, out_val, stream, causal ? m : 0,
                    start);
+}
+
+int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s, void* stream) {
+  if (!x || !y || !s) return DSV32_ERR_INVALID_ARG;
+  if (rows < 0) return DSV32_ERR_INVALID_ARG;
+  if (x_dtype != DSV32_F32 && x_dtype != DSV32_BF16 && x_dtype != DSV32_F16) return DSV32_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(y) || (reinterpret_cast<uintptr_t>(s) & 3u) != 0) return DSV32_ERR_INVALID_ARG;
+  if (rows == 0) return DSV32_OK;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+  using namespace dsv32;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // 4 vectors per warp slot, 8 warps per CTA; one resident wave of CTAs loops over the rest
+  const int64_t want = (rows + 31) / 32;
+  const int64_t cap = static_cast<int64_t>(info->num_sms) * 4;  // 4 resident CTAs per SM (64 registers)
+  const unsigned g = static_cast<unsigned>(want < cap ? want : cap);
+  const char* what = "rotate_quant_kernel launch";
+  if (x_dtype == DSV32_F32)
+    return launch(rotate_quant_kernel<float>, g, kRqThreads, 0, st, what, static_cast<const float*>(x), y, s, rows,
+                  rotate);
+  if (x_dtype == DSV32_BF16)
+    return launch(rotate_quant_kernel<__nv_bfloat16>, g, kRqThreads, 0, st, what,
+                  static_cast<const __nv_bfloat16*>(x), y, s, rows, rotate);
+  return launch(rotate_quant_kernel<__half>, g, kRqThreads, 0, st, what, static_cast<const __half*>(x), y, s, rows,
+                rotate);
+}
+
+int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t* wq, float* ws, void* stream) {
+  if (!w || !wq || !ws) return DSV32_ERR_INVALID_ARG;
+  if (n < 0 || k < 0) return DSV32_ERR_INVALID_ARG;
+  if (n % 128 != 0 || k % 128 != 0) return DSV32_ERR_UNSUPPORTED;
+  if (w_dtype != DSV32_F32 && w_dtype != DSV32_BF16 && w_dtype != DSV32_F16) return DSV32_ERR_INVALID_ARG;
+  if (!aligned16(w) || !aligned16(wq) || (reinterpret_cast<uintptr_t>(ws) & 3u) != 0) return DSV32_ERR_INVALID_ARG;
+  const int64_t blocks = (n / 128) * (k / 128);
+  if (blocks == 0) return DSV32_OK;
+  if (blocks > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
+  int dev = 0;
+  DeviceInfo* info = nullptr;
+  if (int st = device_setup(&dev, &info)) return st;
+  using namespace dsv32;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+  const char* what = "weight_quant_kernel launch";
+  if (w_dtype == DSV32_F32)
+    return launch(weight_quant_kernel<float>, g, kWqThreads, 0, st, what, static_cast<const float*>(w), wq, ws, n, k);
+  if (w_dtype == DSV32_BF16)
+    return launch(weight_quant_kernel<__nv_bfloat16>, g, kWqThreads, 0, st, what,
+                  static_cast<const __nv_bfloat16*>(w), wq, ws, n, k);
+  return launch(weight_quant_kernel<__half>, g, kWqThreads, 0, st, what, static_cast<const __half*>(w), wq, ws, n,
+                k);
 }
 
 int dsv32_device_status(int device, uint32_t* code) {

@@ -197,3 +197,37 @@ def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_score
                                                  topk, int(key_offset), idx.data_ptr(), vals.data_ptr(), s),
                        "int8_index_topk")
     return (scores, idx, vals) if return_scores else (idx, vals)
+
+
+def rotate_quant(x: torch.Tensor, rotate: bool = True):
+    """The indexer's operand producer: x [..., 128] fp32/bf16/fp16 -> (int8 [..., 128], fp32 [...]).
+    Each 128-vector is rotated by the Hadamard transform scaled by 128^-1/2 (rotate=True) and
+    quantised with one scale per vector (hadamard_quant.py:63-103), in the row-major layout
+    int8_index reads."""
+    assert x.is_contiguous() and x.shape[-1] == GROUP, "rotate_quant works on 128-value vectors"
+    assert x.dtype in _DT, f"rotate_quant supports float32/bfloat16/float16, got {x.dtype}"
+    _require_cuda(x)
+    rows = x.numel() // GROUP
+    y = torch.empty(x.shape, device=x.device, dtype=torch.int8)
+    s = torch.empty(x.shape[:-1], device=x.device, dtype=torch.float32)
+    if rows:
+        with _OnDevice(x):
+            _lib.check(_lib.load().dsv32_rotate_quant(x.data_ptr(), _DT[x.dtype], rows, int(bool(rotate)),
+                                                      y.data_ptr(), s.data_ptr(), _stream(x)), "rotate_quant")
+    return y, s
+
+
+def weight_quant(w: torch.Tensor):
+    """GEMM weight block quantiser: w [N, K] fp32/bf16/fp16 -> (int8 [N, K], fp32 [N // 128, K // 128]),
+    one scale max(amax, 1e-4) / 127 per 128 x 128 block (test_kernels.py:80-82, bench.py:43-44)."""
+    assert w.is_contiguous() and w.dim() == 2 and w.shape[0] % GROUP == 0 and w.shape[1] % GROUP == 0
+    assert w.dtype in _DT, f"weight_quant supports float32/bfloat16/float16, got {w.dtype}"
+    _require_cuda(w)
+    N, K = w.shape
+    wq = torch.empty(N, K, device=w.device, dtype=torch.int8)
+    ws = torch.empty(N // GROUP, K // GROUP, device=w.device, dtype=torch.float32)
+    if N and K:
+        with _OnDevice(w):
+            _lib.check(_lib.load().dsv32_weight_quant(w.data_ptr(), _DT[w.dtype], N, K, wq.data_ptr(), ws.data_ptr(),
+                                                      _stream(w)), "weight_quant")
+    return wq, ws

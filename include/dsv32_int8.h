@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define DSV32_ABI_VERSION 3
+#define DSV32_ABI_VERSION 4
 
 /* Status codes. */
 #define DSV32_OK 0
@@ -84,7 +84,7 @@ int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b,
  *    threads) race and must be serialised by the caller.
  *  - Problems with at least one wave of 128-row tiles (one per SM) need no scratch and run at any
  *    size. Smaller problems spread their K blocks over all SMs through the scratch; those that
- *    would need more than 10 MiB (for example m = 64 with n = 7168) return DSV32_ERR_UNSUPPORTED,
+ *    would need more than 10 MiB (for example m = 128 with n = 7168) return DSV32_ERR_UNSUPPORTED,
  *    with the needed size in dsv32_last_error_message(). */
 int dsv32_int8_gemm_noalloc(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c,
                             int c_dtype, int64_t m, int64_t n, int64_t k, void* stream);
@@ -129,6 +129,20 @@ const char* dsv32_status_string(int status);
 
 /* Text of the last CUDA error seen by an entry point on this host thread (static per thread). */
 const char* dsv32_last_error_message(void);
+
+/* Indexer operand producer: replaces hadamard_quant.py:84-103 rotate_quant_kmajor / fwht_quant_kmajor
+ * (row-major output; the K-major packing of kernels_v2 is a host-side view). x [rows, 128] of
+ * x_dtype (DSV32_F32 / DSV32_BF16 / DSV32_F16), 16-byte aligned. rotate != 0: each vector is
+ * multiplied by the 128-point Hadamard matrix scaled by 128^-1/2 (butterfly form, fp32), then
+ * quantised per vector: s[r] = max(amax, 1e-4) * fl32(1/127), y[r, :] = clamp(rint(x / s), -127, 127)
+ * (hadamard_quant.py:63-81). rotate == 0: the quantisation alone. y int8 [rows, 128], s fp32 [rows]. */
+int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s, void* stream);
+
+/* Weight block quantiser for the GEMM's B operand (test_kernels.py:80-82, bench.py:43-44; the
+ * reference computes it inline in torch): w [n, k] of w_dtype, n % 128 == 0, k % 128 == 0, 16-byte
+ * aligned. Per 128 x 128 block: ws = max(amax, 1e-4) / 127 (fp32 division), wq = clamp(rint(w / ws),
+ * -127, 127). wq int8 [n, k], ws fp32 [n/128, k/128]. */
+int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t* wq, float* ws, void* stream);
 
 /* DSV32_ABI_VERSION of the loaded library. */
 int dsv32_abi_version(void);

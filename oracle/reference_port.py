@@ -170,6 +170,23 @@ def rotate_quant_ref(x: np.ndarray, rotate: bool = True):
     return q, s.astype(np.float32)
 
 
+def weight_quant_ref(w: np.ndarray):
+    """The weight block quantiser the reference's tests and benchmark apply to the GEMM's B operand
+    (test_kernels.py:80-82, bench.py:43-44): per 128 x 128 block of w [N, K] (float32), scale =
+    max(amax, 1e-4) / 127 (float32 division), q = clamp(round_half_even(w / scale), -127, 127).
+    Returns (int8 [N, K], float32 [N/128, K/128]). NaN converts to 0."""
+    w = np.asarray(w, dtype=np.float32)
+    N, K = w.shape
+    b = w.reshape(N // GROUP, GROUP, K // GROUP, GROUP)
+    with np.errstate(invalid="ignore"):
+        amax = np.abs(b).max(axis=(1, 3))
+        s = (np.maximum(amax, np.float32(1e-4)) / np.float32(127.0)).astype(np.float32)
+        s = np.where(np.isnan(amax), np.float32(np.nan), s).astype(np.float32)
+        q = np.clip(np.rint(b / s[:, None, :, None]), -127, 127)
+    q = np.nan_to_num(q, nan=0.0).astype(np.int8)
+    return q.reshape(N, K), s
+
+
 def rel_err(x: np.ndarray, ref: np.ndarray) -> float:
     """test_kernels.py:15-17: max |x - ref| over finite ref, divided by max |ref|."""
     x = np.asarray(x, dtype=np.float64)

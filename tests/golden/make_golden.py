@@ -129,6 +129,18 @@ def main(ref_dir: str) -> None:
     vals, inds = torch.topk(sc, 120, dim=-1)
     out["tk_scores"], out["tk_vals"], out["tk_idx"] = sc.numpy(), vals.numpy(), inds.numpy()
 
+    # ---- weight block quantiser: the expressions of test_kernels.py:80-82 / bench.py:43-44 ------
+    g = torch.Generator().manual_seed(80)
+    for wi, (N, K) in enumerate([(256, 384), (128, 1024)]):
+        W = torch.randn(N, K, generator=g) * 0.02
+        W[5, 7] = 3.0  # one outlier block
+        W[:128, 128:256] = 0  # an all-zero block: the 1e-4 floor
+        Wb = W.view(N // 128, 128, K // 128, 128)
+        ws = (Wb.abs().amax((1, 3)).clamp_min(1e-4) / 127)
+        Wq = torch.round(Wb / ws[:, None, :, None]).clamp(-127, 127).to(torch.int8).view(N, K)
+        out[f"wq_{wi}_w"], out[f"wq_{wi}_q"], out[f"wq_{wi}_s"] = W.numpy(), Wq.numpy(), ws.numpy()
+    out["wq_ncases"] = np.array(2)
+
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({os.path.getsize(OUT) / 1e6:.2f} MB, {len(out)} arrays)")
 

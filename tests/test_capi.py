@@ -38,7 +38,7 @@ def test_library_builds_and_exports_every_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.dsv32_abi_version() == 3
+    assert lib.dsv32_abi_version() == 4
     for code in range(6):
         assert lib.dsv32_status_string(code)
     assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")

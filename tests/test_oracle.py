@@ -132,3 +132,12 @@ def test_rel_err_definition():
     ref = np.array([1.0, -2.0, np.inf, 4.0])
     x = np.array([1.0, -2.0, 5.0, 4.004])
     assert abs(O.rel_err(x, ref) - 0.001) < 1e-12
+
+
+def test_weight_quant_oracle_matches_reference_expressions(golden):
+    """weight_quant_ref against the reference's own block-quantisation expressions
+    (test_kernels.py:80-82, bench.py:43-44), evaluated in torch by make_golden.py."""
+    for wi in range(int(golden["wq_ncases"])):
+        q, s = O.weight_quant_ref(golden[f"wq_{wi}_w"])
+        np.testing.assert_array_equal(s, golden[f"wq_{wi}_s"])
+        np.testing.assert_array_equal(q, golden[f"wq_{wi}_q"])

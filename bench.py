@@ -464,6 +464,212 @@ class IndexWorkload(Workload):
                          f"scaled by visible (query, key) pairs")
 
 
+class ProducerWorkload(Workload):
+    """The operand producers either side of the hot path, HBM-bound: the indexer's Hadamard rotate +
+    quantise of the prefill queries (fp32 [4096 * 64, 128], hadamard_quant.py:63-103) and the GEMM
+    weight block quantiser (fp32 expert-down weight [7168, 2048], test_kernels.py:80-82)."""
+
+    def __init__(self, kind, rank, world):
+        self.kind = kind
+        self.name = kind
+        self.unit = "GB/s"
+        self.dtype = "fp32->int8"
+        if kind == "rotate_quant":
+            self.rows = 4096 * 64
+            self.metric = "rotate_quant GB/s"
+            self.bytes = self.rows * 128 * 5 + self.rows * 4
+        else:
+            self.N, self.K = 7168, 2048
+            self.metric = "weight_quant GB/s"
+            self.bytes = self.N * self.K * 5 + (self.N // 128) * (self.K // 128) * 4
+
+    def config(self):
+        if self.kind == "rotate_quant":
+            return {"workload": f"rotate_quant: Hadamard-128 rotation + per-vector int8 of the prefill queries, "
+                                f"fp32 [{self.rows}, 128]"}
+        return {"workload": f"weight_quant: 128x128 block int8 of the expert-down weight, fp32 [{self.N}, {self.K}]"}
+
+    def make_host(self):
+        g = torch.Generator().manual_seed(3)
+        if self.kind == "rotate_quant":
+            x = torch.randn(self.rows, 128, generator=g)
+            x[:, :4] *= 20
+        else:
+            x = torch.randn(self.N, self.K, generator=g) * 0.02
+        return x
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        self.D = D
+        self.host = self.make_host()
+        self.R = max(2, math.ceil(2 * L2_BYTES / self.bytes))
+        self.sets = [self.host.to(dev) for _ in range(self.R)]
+        self.l2_note = f"{self.R} rotating inputs x {self.bytes / 1e6:.1f} MB"
+
+    def _run(self, x):
+        return self.D.rotate_quant(x) if self.kind == "rotate_quant" else self.D.weight_quant(x)
+
+    def step(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        self._run(self.sets[i % self.R])
+        if ev:
+            ev[1].record()
+
+    def value(self, ms, world):
+        return self.bytes * world / (ms * 1e-3) / 1e9
+
+    def e2e_prepare(self, dev):
+        self.hx = self.host.pin_memory()
+        self.dx = torch.empty_like(self.host, device=dev)
+        y, s = self._run(self.dx)
+        self.hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        self.hs = torch.empty(s.shape, dtype=s.dtype).pin_memory()
+        self.h2d = self.hx.numel() * 4
+        self.d2h = self.hy.numel() + self.hs.numel() * 4
+
+    def e2e_step(self):
+        self.dx.copy_(self.hx, non_blocking=True)
+        y, s = self._run(self.dx)
+        self.hy.copy_(y, non_blocking=True)
+        self.hs.copy_(s, non_blocking=True)
+
+    def roofline(self, kernel_ms, peaks, src, traffic):
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        ach = self.bytes / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": traffic.get(self.name), "peak_note": f"{src} STREAM-style copy",
+                "algorithmic_bytes": self.bytes}
+
+    def cpu_sample(self, seconds):
+        import oracle as O
+        if self.kind == "rotate_quant":
+            rows = 8192
+            x = self.host[:rows].double().numpy()
+            fn = lambda: O.rotate_quant_ref(x)  # noqa: E731
+            b = rows * 128 * 5 + rows * 4
+            what = f"oracle rotate_quant_ref (hadamard_quant.py:106-110) on {rows} of {self.rows} vectors"
+        else:
+            nr = 1024
+            x = self.host[:nr].numpy()
+            fn = lambda: O.weight_quant_ref(x)  # noqa: E731
+            b = nr * self.K * 5 + (nr // 128) * (self.K // 128) * 4
+            what = f"oracle weight_quant_ref (test_kernels.py:80-82) on {nr} of {self.N} rows"
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            fn()
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = time.perf_counter() - t0
+        return b * n / dt / 1e9, f"{what}, {n} reps"
+
+
+class IndexStepWorkload(Workload):
+    """The reference's end-to-end indexer step (bench_indexer_e2e.py:46-58) at the 4096^2 causal
+    prefill: rotate + quantise the 4096 new keys into the int8 cache and the fp32 queries
+    [1, 4096, 64, 128], fold the query scales into the head weights, score, select the top-2048."""
+    higher_is_better = False
+    dtype = "fp32->int8"
+    launches_per_step = 4  # rotate_quant (keys), rotate_quant (queries), int8_index, top-k
+
+    def __init__(self, rank, world, topk=2048):
+        self.B, self.M, self.N, self.H, self.topk = 1, 4096, 4096, 64, topk
+        self.name = "index_step"
+        self.metric = "indexer prefill step ms @4096^2 causal (rotate+quant q/k, scores, top-2048)"
+        self.unit = "ms"
+        self.pairs = sum(m + 1 for m in range(self.M))
+        self.ops = 2.0 * self.pairs * self.H * 128
+
+    def config(self):
+        return {"workload": f"indexer step: B=1 M={self.M} new keys={self.N} H=64 D=128 causal, fp32 q/k, "
+                            f"top-{self.topk}", "visible_pairs": self.pairs}
+
+    def make_host(self):
+        g = torch.Generator().manual_seed(0)
+        q = torch.randn(self.B, self.M, self.H, 128, generator=g)
+        k = torch.randn(self.B, self.N, 128, generator=g)
+        k[..., 0] += 5 * 128 ** 0.5  # shared key offset, as the indexer inputs of the other configs
+        w = torch.rand(self.B, self.M, self.H, generator=g) / self.H
+        return q, k, w
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        self.D = D
+        self.host = self.make_host()
+        q, k, w = (t.to(dev) for t in self.host)
+        self.dev_in = (q, k, w)
+        self.cache = D.KeyCache(self.B, self.N, dev)
+        self.cache.append(k)  # the dominant-kernel replay reads the quantised cache and queries
+        self._qq, qs = D.rotate_quant(q)
+        self._w2 = (w * qs).contiguous()
+        self.l2_note = "one input set of 136 MB (> L2): q 134 MB fp32 is read once per step"
+
+    def step(self, i, ev=None, main_only=False):
+        q, k, w = self.dev_in
+        if main_only:  # the dominant kernel alone: scores of the already quantised cache and queries
+            self.D.int8_index(self._qq, self._w2, self.cache.k, self.cache.k_s, causal=True, start=0)
+            return
+        if ev:
+            ev[0].record()
+        self.cache.length = 0
+        self.D.indexer_step(q, w, self.cache, k, topk=self.topk)
+        if ev:
+            ev[1].record()
+
+    def value(self, ms, world):
+        return ms
+
+    def e2e_prepare(self, dev):
+        self.hin = tuple(t.pin_memory() for t in self.host)
+        self.din = tuple(torch.empty_like(t, device=dev) for t in self.hin)
+        self.hidx = torch.empty(self.B, self.M, self.topk, dtype=torch.int32).pin_memory()
+        self.hval = torch.empty(self.B, self.M, self.topk, dtype=torch.float32).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.hin)
+        self.d2h = self.hidx.numel() * 8
+
+    def e2e_step(self):
+        for d, h in zip(self.din, self.hin):
+            d.copy_(h, non_blocking=True)
+        q, k, w = self.din
+        self.cache.length = 0
+        idx, vals = self.D.indexer_step(q, w, self.cache, k, topk=self.topk)
+        self.hidx.copy_(idx, non_blocking=True)
+        self.hval.copy_(vals, non_blocking=True)
+
+    def roofline(self, kernel_ms, peaks, src, traffic):
+        peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        ach = self.ops / (kernel_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
+                "frac": round(ach / peak, 4), "traffic": traffic.get(self.name),
+                "peak_note": f"dense INT8 = 2 x {src} cuBLAS bf16 burst; the dominant kernel (int8_index) alone, "
+                             f"visible (query, key) pairs", "ops_per_launch": self.ops}
+
+    def cpu_sample(self, seconds):
+        import oracle as O
+        q, k, w = self.host
+        rows = np.linspace(0, self.M - 1, 16).astype(np.int64)
+        t0 = time.perf_counter()
+        n = 0
+        qfull = np.zeros((self.B, self.M, self.H, 128), dtype=np.int8)
+        wfull = np.zeros((self.B, self.M, self.H), dtype=np.float32)
+        while True:
+            kq, ks = O.rotate_quant_ref(k.double().numpy())
+            qq, qs = O.rotate_quant_ref(q[:, rows].double().numpy())
+            qfull[:, rows] = qq
+            wfull[:, rows] = w[:, rows].numpy() * qs
+            O.int8_index_ref(qfull, wfull, kq, ks, causal=True, start=0, rows=rows)
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = (time.perf_counter() - t0) / n
+        sample_pairs = sum(int(m) + 1 for m in rows)
+        ms_full = dt * 1e3 * (self.pairs / sample_pairs)
+        return ms_full, (f"oracle rotate_quant_ref + int8_index_ref on {len(rows)} of {self.M} query rows (all "
+                         f"keys quantised), scaled by visible (query, key) pairs")
+
+
 def make_workload(args, rank, world):
     if args.workload == "gemm_up":
         return GemmWorkload(4096, 2048, 7168, "bf16", rank, world, "expert_up")
@@ -473,6 +679,10 @@ def make_workload(args, rank, world):
         return ActQuantWorkload(2048, 7168, args.aq_dtype, rank, world)
     if args.workload in ("index_prefill", "index_decode", "index_long"):
         return IndexWorkload(args.workload.split("_")[1], rank, world)
+    if args.workload in ("rotate_quant", "weight_quant"):
+        return ProducerWorkload(args.workload, rank, world)
+    if args.workload == "index_step":
+        return IndexStepWorkload(rank, world)
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -495,6 +705,8 @@ def run_reference_arm(args):
         wl.host = (x, B, b_s)
     elif isinstance(wl, ActQuantWorkload):
         wl.host = W.act_quant_input(wl.M, wl.N).to(wl.tdt)
+    elif hasattr(wl, "make_host"):
+        wl.host = wl.make_host()
     else:
         wl.host = W.index_inputs(wl.B, wl.M, wl.N, seed=0)
     per = args.ref_step_seconds
@@ -680,7 +892,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gemm_up",
-                    choices=["gemm_up", "gemm_down", "act_quant", "index_prefill", "index_decode", "index_long"])
+                    choices=["gemm_up", "gemm_down", "act_quant", "index_prefill", "index_decode", "index_long",
+                             "rotate_quant", "weight_quant", "index_step"])
     ap.add_argument("--m", type=int, default=32, help="M for gemm_down")
     ap.add_argument("--out", default="bf16", choices=["bf16", "fp32"], help="output dtype for gemm_down")
     ap.add_argument("--aq-dtype", default="fp32", choices=["fp32", "bf16"])

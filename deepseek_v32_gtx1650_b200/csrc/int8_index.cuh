@@ -301,12 +301,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         sWw[e] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (e % H)) : 0.f;
       }
       __syncwarp();
-      float* out_b = out + static_cast<int64_t>(un.b) * M * N;
+      // Per unit: this thread's key column, its k_s and output pointers, and per query the last
+      // visible tile offset (so the per-tile work has no 64-bit arithmetic).
+      const int n_base = wq * 32 + lane;
+      const float* ksp = k_s + static_cast<int64_t>(un.b) * N + n_base;
+      float* outp[C::kQPerWarp];
+      int lim[C::kQPerWarp];  // the key of tile offset t is visible to query q iff t <= lim[q]
+#pragma unroll
+      for (int q = 0; q < C::kQPerWarp; ++q) {
+        const int m = un.m0 + q_first + q;
+        outp[q] = (m < M) ? out + (static_cast<int64_t>(un.b) * M + m) * N + n_base : nullptr;
+        const long long l = causal ? start + m - n_base : 0x7FFFFFFFLL;
+        lim[q] = static_cast<int>(l < -1 ? -1 : (l > 0x7FFFFFFFLL ? 0x7FFFFFFFLL : l));
+      }
       for (int kt = un.kt0; kt < un.kt_vis; ++kt, ++i) {
         const uint32_t buf = i & 1u;
-        const int n = kt * kKeysPerTile + wq * 32 + lane;
+        const int toff = kt * kKeysPerTile;
+        const bool n_ok = toff + n_base < N;
         // k_s * 2^22 undoes the 2^-22 of the relu step (power-of-two scalings: same rounding).
-        const float ks = (n < N) ? __ldg(k_s + static_cast<int64_t>(un.b) * N + n) * 0x1p22f : 0.f;
+        const float ks = n_ok ? __ldg(ksp + toff) * 0x1p22f : 0.f;
         if (!mbar_wait_warp(tfull_bar(buf), (i >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
           ok = false;
           break;
@@ -339,14 +352,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[q][1] = __ffma2_rn(v1, make_float2(w4.z, w4.w), acc[q][1]);
           }
         }
-        if (n < N) {
+        if (n_ok) {
 #pragma unroll
           for (int q = 0; q < C::kQPerWarp; ++q) {
-            const int m = un.m0 + q_first + q;
-            if (m < M) {
+            if (outp[q]) {
               float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
-              if (causal && static_cast<long long>(n) > start + m) sc = -INFINITY;
-              out_b[static_cast<int64_t>(m) * N + n] = sc;
+              if (toff > lim[q]) sc = -INFINITY;
+              outp[q][toff] = sc;
             }
           }
         }

@@ -8,7 +8,8 @@ bf16 out, per GPU. With N GPUs (torchrun, one rank per GPU) the weight is sharde
 N = 2048 * world, each rank computes its own 2048 columns (weak scaling, no data-path collective).
 Other workloads: gemm_down (K=2048 N=7168, --m), act_quant (fp32/bf16 [2048, 7168]),
 index_prefill (4096 x 4096 causal, scores + top-2048), index_decode (4 x 32768 + top-2048),
-index_long (4096 queries x 131072 keys causal, keys sharded by range, all-gather merge).
+index_long (4096 queries x 131072 keys causal, keys sharded by range, per-shard top-2048 merged by
+query row after an NCCL all-to-all, merged rows all-gathered).
 
 Timing: W untimed warm-up steps, then K steps between a barrier + synchronize on both sides,
 CUDA events on the launching stream, max over ranks. Inputs rotate over enough copies to exceed
@@ -356,8 +357,9 @@ class IndexWorkload(Workload):
         rows = self.B * self.M
         nloc = (self.N + world - 1) // world if kind == "long" else self.N
         self.launches_per_step = 1 + topk_launches(rows, nloc, topk)
-        if kind == "long" and world > 1:
-            self.launches_per_step += topk_launches(rows, world * topk, topk)
+        if kind == "long" and world > 1:  # merge: rows / world rows per rank when they split evenly
+            mrows = rows // world if rows % world == 0 else rows
+            self.launches_per_step += topk_launches(mrows, world * topk, topk)
 
     def config(self):
         return {"workload": f"lightning indexer {self.kind}: B={self.B} M={self.M} N={self.N} H=64 D=128 "

@@ -269,28 +269,13 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) neg_nan |= (pos0 + i < valid) && key[i] < kNegInfKey;
     if (!__syncthreads_or(neg_nan)) {  // (the barrier also orders the histogram clear above)
+      // Output j is position j: a coalesced copy (the visible scores are re-read from L1 / L2).
       const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
       int32_t* oi = out_idx + out_row * k;
       float* ov = out_val + out_row * k;
-      const bool staged = k <= kStageMax;
-#pragma unroll
-      for (int i = 0; i < ITEMS; ++i) {
-        const int pos = pos0 + i;
-        if (pos < k) {
-          const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + seg0 + idx_offset);
-          const float x = fkey_inv(key[i]);
-          if (staged) {
-            sh.u.out.idx[pos] = id;
-            sh.u.out.val[pos] = x;
-          } else {
-            oi[pos] = id;
-            ov[pos] = x;
-          }
-        }
-      }
-      if (staged) {
-        __syncthreads();
-        copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
+      for (int j = tid; j < k; j += THREADS) {
+        oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
+        ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
       }
       return;
     }

@@ -6,11 +6,16 @@ Only the two paths that shard naturally are partitioned:
   B and b_s); A and a_s are replicated. The kernel needs no collective. gather_columns()
   optionally all-gathers the column slices into the full [M, N] output.
 - The indexer by key range: rank r owns keys [lo, hi) of the key cache (lo a multiple of 128).
-  It scores every query against its keys with the causal limit shifted by -lo, selects its local
-  top-k (global key ids = lo + position), and the (value, id) lists are all-gathered over
-  NVLink. Every rank then merges the world * k candidates with the same top-k kernel. Local lists
-  are position-ordered and concatenated in rank order, so ties resolve to the lowest global key
-  id exactly as in the single-GPU selection; the merged result is identical to it.
+  It scores every query against its keys with the causal limit shifted by -lo and selects its
+  local top-k (global key ids = lo + position). The lists are then merged by query row: an
+  all-to-all over NVLink hands rank r the lists of its 1/world of the rows from every rank, it
+  merges those rows' world * k candidates with the same top-k kernel, and an all-gather of the
+  merged rows gives every rank the whole result. Each rank moves about 2 * rows * k * 8 bytes and
+  merges rows / world rows, whatever the world size (gathering every list to every rank moves
+  world times that and merges every row everywhere; it remains the path when the rows do not
+  split evenly). Local lists are position-ordered and concatenated in rank order, so ties resolve
+  to the lowest global key id exactly as in the single-GPU selection; the merged result is
+  identical to it.
 
 The reference has no multi-GPU code (single GTX 1650); these are the two exchange patterns its
 hot path admits.
@@ -52,6 +57,45 @@ def gather_candidates(idx: torch.Tensor, vals: torch.Tensor, group=None):
     return cand[0].contiguous(), cand[1].contiguous().view(torch.float32)
 
 
+def _select(cand_val, topk, cand_idx):
+    return K.select_topk(cand_val, topk, cand_idx=cand_idx)
+
+
+def merge_candidates(idx: torch.Tensor, vals: torch.Tensor, topk: int, group=None, merge=None):
+    """Merge per-rank top-k lists ([rows, k] int32 global ids, [rows, k] fp32 values; every rank
+    holds the same rows) into the top-`topk` of each row over all ranks, returned on every rank as
+    ([rows, topk] int32, [rows, topk] fp32). `merge(cand_val, topk, cand_idx)` selects over a row's
+    candidates (default: the top-k kernel); it is a parameter so the exchange logic can be checked
+    against a CPU selection.
+
+    rows divisible by the world size: rows are split into equal blocks; two all-to-alls (ids, value
+    bits) give each rank every rank's lists for its block, it merges them, and two all-gathers
+    assemble the merged blocks. Otherwise every list is all-gathered and every rank merges all rows.
+    Either way a row's candidates are the ranks' lists concatenated in rank order."""
+    merge = merge or _select
+    world = dist.get_world_size(group)
+    rows, k = idx.shape
+    if world == 1:
+        return (idx, vals) if topk == k else merge(vals, topk, idx)
+    if rows % world:
+        cidx, cval = gather_candidates(idx, vals, group)
+        return merge(cval, topk, cidx)
+    r = rows // world
+    ids_in = torch.empty(world * r * k, dtype=torch.int32, device=idx.device)
+    bits_in = torch.empty(world * r * k, dtype=torch.int32, device=idx.device)
+    dist.all_to_all_single(ids_in, idx.contiguous().view(-1), group=group)
+    dist.all_to_all_single(bits_in, vals.contiguous().view(torch.int32).view(-1), group=group)
+    # source-rank-major [world, r, k] -> per row, the ranks' lists in rank order [r, world * k]
+    cidx = ids_in.view(world, r, k).permute(1, 0, 2).reshape(r, world * k)
+    cval = bits_in.view(world, r, k).permute(1, 0, 2).reshape(r, world * k).view(torch.float32)
+    mi, mv = merge(cval, topk, cidx)
+    out_i = torch.empty(rows, topk, dtype=torch.int32, device=idx.device)
+    out_b = torch.empty(rows, topk, dtype=torch.int32, device=idx.device)
+    dist.all_gather_into_tensor(out_i, mi.contiguous(), group=group)
+    dist.all_gather_into_tensor(out_b, mv.contiguous().view(torch.int32), group=group)
+    return out_i, out_b.view(torch.float32)
+
+
 def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, causal: bool = False,
                        start: int = 0, group=None):
     """Key-range sharded indexer + top-k. q [B, M, H, D], w [B, M, H] replicated; k_local [B, n_r, D],
@@ -62,8 +106,7 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
                                   start=local_causal_start(start, key_lo), return_scores=False,
                                   key_offset=key_lo)
-    cidx, cval = gather_candidates(idx.view(B * M, topk), vals.view(B * M, topk), group)
-    midx, mval = K.select_topk(cval, topk, cand_idx=cidx)
+    midx, mval = merge_candidates(idx.view(B * M, topk), vals.view(B * M, topk), topk, group)
     return midx.view(B, M, topk), mval.view(B, M, topk)
 
 

@@ -105,3 +105,18 @@ def test_act_quant_large_input_edge_cases(golden, dt, n):
         np.testing.assert_array_equal(npy(s), sr)
         np.testing.assert_array_equal(npy(y), yr)
     assert_no_device_error()
+
+
+@pytest.mark.parametrize("rs", [True, False])
+def test_act_quant_all_ties_large(rs):
+    """Every value an exact (ue8m0) or near (fp32 scale) rounding tie, on a multi-wave input: every
+    lane takes the exact path for more groups than it remembers, so the warp-wide redo runs too."""
+    g = torch.Generator().manual_seed(12)
+    n = torch.randint(-127, 127, (2048, 7168), generator=g).float()
+    x = (n + 0.5) * 0.125
+    x.view(-1, 128)[:, 0] = 127 * 0.125  # amax of every group: ue8m0 scale exactly 2^-3
+    y, s = D.act_quant(x.to(DEV), rs)
+    yr, sr = O.act_quant_ref(x.numpy(), rs)
+    np.testing.assert_array_equal(npy(s), sr)
+    np.testing.assert_array_equal(npy(y), yr)
+    assert_no_device_error()

@@ -1,9 +1,10 @@
 """Multi-rank host logic of the sharded paths on CPU: two gloo ranks in spawned processes.
 
 The indexer is split by key range; every rank scores its keys with the causal limit shifted by
-its first key, keeps a local top-k with global key ids, and the lists are all-gathered and merged.
-Here the per-rank compute is the CPU oracle; the sharding helpers (shard_range, the causal shift,
-gather_candidates, gather_columns) are the product's. The merged selection must equal the
+its first key, keeps a local top-k with global key ids, and the lists are exchanged and merged
+(all-to-all by query row when the rows split evenly, else all-gather). Here the per-rank compute
+and the row selection are the CPU oracle; the sharding helpers (shard_range, the causal shift,
+merge_candidates, gather_candidates, gather_columns) are the product's. The merged selection must equal the
 single-process top-k exactly, for several world sizes and causal offsets. A rank that fails before
 the collective must make its peer's collective fail (short timeout), not hang it.
 """
@@ -41,6 +42,11 @@ def _merge_oracle(cand_idx, cand_val, k):
     return ids, vals
 
 
+def _oracle_select(cand_val, k, cand_idx):
+    ids, vals = _merge_oracle(cand_idx.numpy(), cand_val.numpy(), k)
+    return torch.from_numpy(ids.astype(np.int32)), torch.from_numpy(vals.astype(np.float32))
+
+
 def _index_worker(rank, world, port, M, N, k, causal, start, q):
     try:
         _init(rank, world, port)
@@ -51,8 +57,7 @@ def _index_worker(rank, world, port, M, N, k, causal, start, q):
         li, lv = O.topk_ref(sc, k)
         idx = torch.from_numpy((li + lo).astype(np.int32))
         val = torch.from_numpy(lv.astype(np.float32))
-        cidx, cval = S.gather_candidates(idx, val)
-        mi, mv = _merge_oracle(cidx.numpy(), cval.numpy(), k)
+        mi, mv = (t.numpy() for t in S.merge_candidates(idx, val, k, merge=_oracle_select))
         full = O.int8_index_ref(qi.numpy(), w.numpy(), keys.numpy(), ks.numpy(), causal=causal,
                                 start=start)[0].astype(np.float32)
         gi, gv = O.topk_ref(full, k)
@@ -77,9 +82,12 @@ def _run(target, world, *args):
     return sorted(res)
 
 
-@pytest.mark.parametrize("world,causal,start", [(2, False, 0), (2, True, 700), (3, True, 300), (4, True, 0)])
-def test_key_sharded_topk_merge_equals_single_process(world, causal, start):
-    M, N, k = 12, 1024, 64
+# M = 12 splits evenly over 2, 3 and 4 ranks (all-to-all by row); M = 10 over 4 and M = 13 over 3
+# do not (all-gather)
+@pytest.mark.parametrize("world,M,causal,start", [(2, 12, False, 0), (2, 12, True, 700), (3, 12, True, 300),
+                                                  (4, 12, True, 0), (4, 10, True, 500), (3, 13, False, 0)])
+def test_key_sharded_topk_merge_equals_single_process(world, M, causal, start):
+    N, k = 1024, 64
     res = _run(_index_worker, world, M, N, k, causal, start)
     assert all(ok for _, ok, _ in res), res
 

@@ -13,7 +13,7 @@
 //
 // weight_quant: the GEMM's B operand (test_kernels.py:80-82, bench.py:43-44): per 128 x 128 block
 //   of W [N, K], s = max(amax, 1e-4) / 127 (an fp32 division), y = clamp(rint(x / s), -127, 127);
-//   scales [N/128, K/128]. One CTA per block; each thread keeps 64 values in registers.
+//   scales [N/128, K/128]. One CTA of 512 threads per block; each thread keeps 32 values in registers.
 //
 // Both use act_quant's exact rounding (aq_quant_lane): rint(fl(x / s)) without a per-value
 // division, valid for any scale s with |x / s| <= 127 + tiny.
@@ -23,7 +23,7 @@
 namespace dsv32 {
 
 constexpr int kRqThreads = 256;
-constexpr int kWqThreads = 256;
+constexpr int kWqThreads = 512;
 
 // 16 consecutive values of a 128-vector (16-bit or fp32 source) into fp32 registers.
 template <typename T>
@@ -52,7 +52,7 @@ DSV32_DEV uint4 pack16(const uint32_t (&q)[16]) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kRqThreads) rotate_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
+__global__ void __launch_bounds__(kRqThreads, 4) rotate_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
                                                                    float* __restrict__ s, int64_t rows, int rotate) {
   constexpr int LPV = 8;          // lanes per vector
   constexpr int VPW = 32 / LPV;   // vectors per warp slot
@@ -74,26 +74,37 @@ __global__ void __launch_bounds__(kRqThreads) rotate_quant_kernel(const T* __res
       for (int i = 0; i < 16; ++i) v[i] = 0.f;
     }
     if (rotate) {
-      // strides 1, 2, 4, 8: pairs inside this lane's 16 values
+      // strides 1, 2, 4, 8: pairs inside this lane's 16 values, two butterflies per packed f32x2
+      // add (a + b) and packed fma (b * -1 + a = a - b, one rounding like the subtraction)
+      const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
       for (int st = 1; st < 16; st <<= 1) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          if ((i & st) == 0) {
-            const float a = v[i], b = v[i + st];
-            v[i] = a + b;
-            v[i + st] = a - b;
+          if ((i & st) == 0 && ((i / st) & 2) == 0) {  // butterflies (i, i + st) and (j, j + st), j = i + 2 st
+            const int j = (st == 8) ? i + 1 : i + 2 * st;
+            if (st == 8 && (i & 1)) continue;
+            const float2 a = make_float2(v[i], v[j]), b = make_float2(v[i + st], v[j + st]);
+            const float2 sum = __fadd2_rn(a, b), dif = __ffma2_rn(b, neg1, a);
+            v[i] = sum.x;
+            v[j] = sum.y;
+            v[i + st] = dif.x;
+            v[j + st] = dif.y;
           }
         }
       }
-      // strides 16, 32, 64: the partner value sits in lane sl ^ m of the same vector
+      // strides 16, 32, 64: the partner value sits in lane sl ^ m of the same vector; the low lane
+      // keeps v + o and the high lane o - v, both as fma(sign, v, o) (exact sign, one rounding)
 #pragma unroll
       for (int m = 1; m < LPV; m <<= 1) {
-        const bool hi = (sl & m) != 0;
+        const float sg = (sl & m) ? -1.f : 1.f;
+        const float2 sg2 = make_float2(sg, sg);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-          v[i] = hi ? (o - v[i]) : (v[i] + o);
+        for (int i = 0; i < 16; i += 2) {
+          const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, v[i], m), __shfl_xor_sync(0xffffffffu, v[i + 1], m));
+          const float2 r = __ffma2_rn(make_float2(v[i], v[i + 1]), sg2, o);
+          v[i] = r.x;
+          v[i + 1] = r.y;
         }
       }
       constexpr float kInvSqrt128 = 0.08838834764831845f;  // fl32(128^-1/2)
@@ -116,25 +127,26 @@ __global__ void __launch_bounds__(kRqThreads) rotate_quant_kernel(const T* __res
   }
 }
 
-// One CTA per 128 x 128 block of W [n, k]: thread t holds row t / 2, columns 64 * (t % 2) ...
+// One CTA per 128 x 128 block of W [n, k]: thread t holds row t / 4, the 16-value chunks t % 4 and
+// t % 4 + 4 of it (four threads read a row's 128 values as two contiguous 256-byte runs).
 template <typename T>
-__global__ void __launch_bounds__(kWqThreads) weight_quant_kernel(const T* __restrict__ w, int8_t* __restrict__ wq,
+__global__ void __launch_bounds__(kWqThreads, 2) weight_quant_kernel(const T* __restrict__ w, int8_t* __restrict__ wq,
                                                                   float* __restrict__ ws, int64_t n, int64_t k) {
   __shared__ float red[kWqThreads / 32];
   const int tid = threadIdx.x;
   const int64_t kb_count = k / 128;
   const int64_t nb = blockIdx.x / kb_count;
   const int64_t kb = blockIdx.x % kb_count;
-  const int64_t row = nb * 128 + tid / 2;
-  const int64_t col = kb * 128 + (tid % 2) * 64;
+  const int64_t row = nb * 128 + tid / 4;
+  const int64_t col = kb * 128 + (tid % 4) * 16;
   pdl_wait();
   pdl_launch_dependents();
-  float v[64];
+  float v[32];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) load16(w + row * k + col + 16 * j, *reinterpret_cast<float(*)[16]>(v + 16 * j));
+  for (int j = 0; j < 2; ++j) load16(w + row * k + col + 64 * j, *reinterpret_cast<float(*)[16]>(v + 16 * j));
   float a = 0.f;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) a = max_nan(a, fabsf(v[i]));
+  for (int i = 0; i < 32; ++i) a = max_nan(a, fabsf(v[i]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
   if ((tid & 31) == 0) red[tid >> 5] = a;
@@ -146,9 +158,9 @@ __global__ void __launch_bounds__(kWqThreads) weight_quant_kernel(const T* __res
   const float rc = rcp_1ulp(sc);
   uint32_t q[16];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 2; ++j) {
     aq_quant_lane<16>(*reinterpret_cast<const float(*)[16]>(v + 16 * j), sc, rc, q);
-    *reinterpret_cast<uint4*>(wq + row * k + col + 16 * j) = pack16(q);
+    *reinterpret_cast<uint4*>(wq + row * k + col + 64 * j) = pack16(q);
   }
   if (tid == 0) ws[nb * kb_count + kb] = sc;
 }

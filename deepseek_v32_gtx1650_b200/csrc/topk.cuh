@@ -280,8 +280,178 @@ __global__ void __launch_bounds__(THREADS) topk_reg_kernel(const float* __restri
       return;
     }
   }
-  // 1. Row statistics behind one barrier (which also orders the histogram clear before pass 1):
-  //    counts above / at the -inf key and the key range of the values above -inf.
+  // 1. Common case, at least k values above -inf (every indexer row past the fast path): statistics of
+  //    the keys above -inf behind one barrier (which also orders the histogram clear before pass 1),
+  //    with keys at or below -inf mapped to the top of the unsigned range for the minimum.
+  {
+    int na = 0;
+    uint32_t mnw = 0xFFFFFFFFu, mx = 0u;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+      na += key[i] > kNegInfKey ? 1 : 0;
+      mnw = min(mnw, key[i] - (kNegInfKey + 1u));
+      mx = max(mx, key[i]);
+    }
+    const uint32_t r0 = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(na));
+    const uint32_t r2 = __reduce_min_sync(0xffffffffu, mnw);
+    const uint32_t r3 = __reduce_max_sync(0xffffffffu, mx);
+    if (lane == 0) {
+      sh.red[0][wid] = r0;
+      sh.red[2][wid] = r2;
+      sh.red[3][wid] = r3;
+    }
+  }
+  __syncthreads();
+  {
+    int above = 0;
+    uint32_t mnw = 0xFFFFFFFFu, mx = 0u;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      above += static_cast<int>(sh.red[0][w]);
+      mnw = min(mnw, sh.red[2][w]);
+      mx = max(mx, sh.red[3][w]);
+    }
+    if (above >= k) {
+      // 2. Radix select among the keys above -inf. Past the first pass the open bin is at most 2^21
+      //    keys wide and never straddles the -inf key (a multiple of 2^23 plus 2^23 - 1), so a prefix
+      //    match alone identifies the participants.
+      const uint32_t mn = mnw + (kNegInfKey + 1u);
+      int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);
+      uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
+      int krem = k;
+      uint32_t T = 0u;
+      bool first = true, resolved = false;
+      while (shift > 0) {
+        const int d = min(kRegBits, shift);
+        const int nbins = 1 << d;
+        const int ns = shift - d;
+        if (first) {
+#pragma unroll
+          for (int i = 0; i < ITEMS; ++i)
+            if (key[i] > kNegInfKey) atomicAdd(&sh.u.hist[(key[i] >> ns) & (nbins - 1)], 1);
+        } else {
+          for (int i = tid; i < nbins; i += THREADS) sh.u.hist[i] = 0;
+          __syncthreads();
+          const uint32_t ph = prefix >> shift;
+#pragma unroll
+          for (int i = 0; i < ITEMS; ++i)
+            if ((key[i] >> shift) == ph) atomicAdd(&sh.u.hist[(key[i] >> ns) & (nbins - 1)], 1);
+        }
+        first = false;
+        __syncthreads();
+        const int per = (nbins + THREADS - 1) / THREADS;
+        int local = 0;
+        if ((per & 3) == 0) {
+          const int4* hv = reinterpret_cast<const int4*>(sh.u.hist + (nbins - (tid + 1) * per));
+          for (int j = 0; j < per / 4; ++j) {
+            const int4 h4 = hv[j];
+            local += (h4.x + h4.y) + (h4.z + h4.w);
+          }
+        } else {
+          for (int j = 0; j < per; ++j) {
+            const int bin = nbins - 1 - (tid * per + j);
+            if (bin >= 0) local += sh.u.hist[bin];
+          }
+        }
+        const int before = excl_scan_once<THREADS>(local, sh.scan);
+        if (before < krem && krem <= before + local) {
+          int acc = before;
+          for (int j = 0; j < per; ++j) {
+            const int bin = nbins - 1 - (tid * per + j);
+            const int c = sh.u.hist[bin];
+            if (acc + c >= krem) {
+              sh.prefix = prefix | (uint32_t(bin) << ns);
+              sh.krem = krem - acc;
+              sh.bin_cnt = c;
+              sh.cand_n = 0;
+              break;
+            }
+            acc += c;
+          }
+        }
+        __syncthreads();
+        prefix = sh.prefix;
+        krem = sh.krem;
+        const int cnt = sh.bin_cnt;
+        shift = ns;
+        if (shift > 0 && cnt <= 32) {
+          const uint32_t ph = prefix >> shift;
+#pragma unroll
+          for (int i = 0; i < ITEMS; ++i)
+            if ((key[i] >> shift) == ph) sh.cand[atomicAdd(&sh.cand_n, 1)] = key[i];
+          __syncthreads();
+          if (wid == 0) {
+            const uint32_t mine = lane < cnt ? sh.cand[lane] : 0u;
+            int g = 0, e = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint32_t c = __shfl_sync(0xffffffffu, mine, j);
+              g += (j < cnt && c > mine) ? 1 : 0;
+              e += (j < cnt && c == mine) ? 1 : 0;
+            }
+            if (lane < cnt && g < krem && krem <= g + e) {
+              sh.T = mine;
+              sh.krem = krem - g;
+            }
+          }
+          __syncthreads();
+          T = sh.T;
+          krem = sh.krem;
+          resolved = true;
+          break;
+        }
+      }
+      if (!resolved) T = prefix;
+      // 3. Ordered compaction; T is above -inf, so masked and padding keys are never selected.
+      uint32_t gmask = 0, emask = 0;
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) {
+        gmask |= key[i] > T ? (1u << i) : 0u;
+        emask |= key[i] == T ? (1u << i) : 0u;
+      }
+      const int eq = __popc(emask);
+      const int packed = excl_scan_once<THREADS>((__popc(gmask) << 16) | eq, sh.scan);  // n <= 65535
+      const int eq_before = packed & 0xFFFF;
+      const int take = max(0, min(eq, krem - eq_before));
+      while (__popc(emask) > take) emask &= ~(0x80000000u >> __clz(emask));  // drop the highest
+      const uint32_t smask = gmask | emask;
+      const int o = (packed >> 16) + min(eq_before, krem);
+      int32_t* oi = out_idx + out_row * k;
+      float* ov = out_val + out_row * k;
+      const bool staged = k <= kStageMax;
+      int32_t* si = staged ? sh.u.out.idx : oi;
+      float* sv = staged ? sh.u.out.val : ov;
+      if (cand_idx) {
+        const int32_t* cand_row = cand_idx + row * cand_ld + seg0;
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+          if (smask & (1u << i)) {
+            const int slot = o + __popc(smask & ((1u << i) - 1u));
+            si[slot] = cand_row[pos0 + i];
+            sv[slot] = fkey_inv(key[i]);
+          }
+        }
+      } else {
+        const int32_t id0 = static_cast<int32_t>(pos0 + seg0 + idx_offset);  // ids are int32
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+          const int slot = o + __popc(smask & ((1u << i) - 1u));
+          if (smask & (1u << i)) {
+            si[slot] = id0 + i;
+            sv[slot] = fkey_inv(key[i]);
+          }
+        }
+      }
+      if (staged) {
+        __syncthreads();
+        copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
+      }
+      return;
+    }
+  }
+  __syncthreads();  // the general path below rewrites the statistics slots read above
+  // General path (fewer than k values above -inf, so masked -inf or negative NaN keys are selected):
+  // row statistics, counts above / at the -inf key and the key range of the values above -inf.
   {
     int na = 0, ni = 0;
     uint32_t mn = 0xFFFFFFFFu, mx = 0u;

@@ -94,20 +94,33 @@ DSV32_DEV float aq_exact_bits(float x, float s) {
 // Applied to the EPL values of one lane with a single (rarely taken) branch: the fast results and one
 // "near a tie / NaN" flag per lane, then the exact path for the flagged values only.
 // Pairs of values use the packed f32x2 FMA: big = x*r + M, -n = big*(-1) + M (exact), t = x*r - n.
-template <int EPL>
+// kSquares selects how the near-tie flag is formed: one packed t * t - c per pair whose sign bits
+// are AND-ed (fewer instructions; [2048, 7168] fp32: 11.6 -> 11.2 us), with c = 1/4 - 2^-14 <
+// bound^2 so that an unflagged value has |t| < bound, and a scale that is not finite (a NaN or
+// infinity in the group) sending the lane to the exact path; or per-value |t| <= bound compares
+// (bf16 input: 11.9 us against 12.1 us for the packed form).
+template <int EPL, bool kSquares = true>
 DSV32_DEV void aq_quant_lane(const float (&f)[EPL], float s, float r, uint32_t (&bits)[EPL]) {
   constexpr float kMagic = 12582912.0f;
   const float2 r2 = make_float2(r, r), m2 = make_float2(kMagic, kMagic), neg1 = make_float2(-1.f, -1.f);
+  const float2 c2 = make_float2(-0.24993896484375f, -0.24993896484375f);
   bool slow = false;
+  uint32_t neg = 0xFFFFFFFFu;
 #pragma unroll
   for (int e = 0; e < EPL; e += 2) {
     const float2 x2 = make_float2(f[e], f[e + 1]);
     const float2 big = __ffma2_rn(x2, r2, m2);
     const float2 t = __ffma2_rn(x2, r2, __ffma2_rn(big, neg1, m2));
-    slow |= !(fabsf(t.x) <= kAqTieBound) || !(fabsf(t.y) <= kAqTieBound);
+    if constexpr (kSquares) {
+      const float2 q = __ffma2_rn(t, t, c2);
+      neg &= __float_as_uint(q.x) & __float_as_uint(q.y);
+    } else {
+      slow |= !(fabsf(t.x) <= kAqTieBound) || !(fabsf(t.y) <= kAqTieBound);
+    }
     bits[e] = __float_as_uint(big.x);
     bits[e + 1] = __float_as_uint(big.y);
   }
+  if constexpr (kSquares) slow = !(neg >> 31) || !(s < INFINITY);
   if (slow) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
@@ -179,7 +192,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
       const float rc = rcp_1ulp(sc);
       if (valid) {
         uint32_t qb[EPL];
-        aq_quant_lane<EPL>(f, sc, rc, qb);
+        aq_quant_lane<EPL, sizeof(T) == 4>(f, sc, rc, qb);
         int8_t* dst = y + g * 128 + sl * EPL;
         if constexpr (EPL == 4) {
           __stcs(reinterpret_cast<unsigned int*>(dst), aq_pack4(qb[0], qb[1], qb[2], qb[3]));

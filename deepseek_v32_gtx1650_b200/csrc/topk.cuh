@@ -219,10 +219,11 @@ DSV32_DEV void copy_out_staged(const int32_t* sidx, const float* sval, int32_t* 
 // [seg0, seg0 + seg_len) of input row r' / nseg); nseg = 1, seg_len = n_total is the plain top-k.
 // Each segment's list is written to out row r' (k entries); the nseg lists of an input row are
 // contiguous, in segment order, so they form that row's candidate list for a merge pass.
-// 256-thread rows run six CTAs per SM (40 registers, a few spilled): the barriers between the
-// selection phases are hidden by the other CTAs (4096 x 4096: 57.4 -> 53.1 us against four CTAs).
+// Six 256-thread or three 512-thread CTAs per SM (40 registers, some spilled to L1): the barriers
+// between the selection phases are hidden by the other CTAs (4096 x 4096: 57.4 -> 53.1 us against
+// four 256-thread CTAs; 2048 x 131072 staged: 1593 -> 1461 us against two 512-thread CTAs).
 template <int THREADS, int ITEMS>
-__global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 2) topk_reg_kernel(const float* __restrict__ vals, long long ld, int n_total,
+__global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kernel(const float* __restrict__ vals, long long ld, int n_total,
                                                            const int32_t* __restrict__ cand_idx, long long cand_ld,
                                                            long long idx_offset, int k, int32_t* __restrict__ out_idx,
                                                            float* __restrict__ out_val, int causal_m,

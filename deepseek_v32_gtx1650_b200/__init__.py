@@ -7,7 +7,7 @@ The kernels live in libdsv32_int8.so (C ABI: include/dsv32_int8.h), built in-tre
 `python -m deepseek_v32_gtx1650_b200.build`.
 """
 from .kernels import (GROUP, act_quant, int8_gemm, int8_gemm_partials, int8_index, int8_index_topk,
-                      rotate_quant, select_topk, weight_quant)
+                      rotate_quant, select_topk, select_topk_parts, weight_quant)
 from .kernels_v2 import (act_quant_kmajor, index_kmajor_k, index_kmajor_q, int8_gemm_v2, int8_index_v2, kmajor,
                          unkmajor)
 from .hadamard_quant import fwht_quant_kmajor, hadamard_matrix, rotate_quant_kmajor, unpack_kmajor
@@ -16,6 +16,7 @@ from ._lib import Dsv32Error, device_status
 
 __all__ = [
     "GROUP", "act_quant", "int8_gemm", "int8_gemm_partials", "int8_index", "int8_index_topk", "select_topk",
+    "select_topk_parts",
     "act_quant_kmajor", "kmajor", "unkmajor", "int8_gemm_v2", "index_kmajor_q", "index_kmajor_k", "int8_index_v2",
     "rotate_quant", "weight_quant", "rotate_quant_kmajor", "fwht_quant_kmajor", "hadamard_matrix", "unpack_kmajor",
     "KeyCache", "indexer_step", "Dsv32Error", "device_status",

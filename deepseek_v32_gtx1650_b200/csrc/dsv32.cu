@@ -329,7 +329,8 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
 // (nseg = 1: whole rows of length n), k selections per segment into out [rows * nseg, k].
 int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
                     int64_t idx_offset, int k, int32_t* out_idx, float* out_val, int causal_m, int64_t causal_start,
-                    int64_t causal_row0, int seg_len, int nseg, cudaStream_t st) {
+                    int64_t causal_row0, int seg_len, int nseg, cudaStream_t st,
+                    const dsv32::topk::RowParts& parts = dsv32::topk::RowParts{}) {
   using namespace dsv32::topk;
   const int64_t grid = rows * nseg;
   if (grid > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
@@ -338,12 +339,12 @@ int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const in
   const char* what = "topk kernel launch";
   if (seg_len <= 256 * 4)
     return launch(topk_reg_kernel<256, 4>, g, 256, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx,
-                  out_val, causal_m, cs, cr0, seg_len, nseg);
+                  out_val, causal_m, cs, cr0, seg_len, nseg, parts);
   if (seg_len <= 256 * 16)
     return launch(topk_reg_kernel<256, 16>, g, 256, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k,
-                  out_idx, out_val, causal_m, cs, cr0, seg_len, nseg);
+                  out_idx, out_val, causal_m, cs, cr0, seg_len, nseg, parts);
   return launch(topk_reg_kernel<512, 16>, g, 512, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx,
-                out_val, causal_m, cs, cr0, seg_len, nseg);
+                out_val, causal_m, cs, cr0, seg_len, nseg, parts);
 }
 
 constexpr int kTopkRegMax = 512 * 16;                  // longest row a register pass holds
@@ -361,9 +362,11 @@ constexpr int64_t kTopkTempBytes = int64_t(256) << 20;  // stream-ordered scratc
 // shorter than k, the long-row kernel re-reads the row from L2 instead.
 int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream, int64_t causal_m = 0,
-              int64_t causal_start = 0) {
-  if (!scores || !out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
-  if (rows < 1 || n < 1 || k < 1 || k > n || ld < n) return DSV32_ERR_INVALID_ARG;
+              int64_t causal_start = 0, const dsv32::topk::RowParts* parts = nullptr) {
+  const dsv32::topk::RowParts no_parts{};
+  const dsv32::topk::RowParts& p0 = parts ? *parts : no_parts;  // addressing of the first pass
+  if ((!scores && !parts) || !out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
+  if (rows < 1 || n < 1 || k < 1 || k > n || (!parts && ld < n)) return DSV32_ERR_INVALID_ARG;
   if (cand_idx && cand_ld < n) return DSV32_ERR_INVALID_ARG;
   if (n > (1LL << 31) - 1 || rows > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
   int dev = 0;
@@ -375,7 +378,7 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   const int cm = causal_m > 0 && causal_m <= 0x7FFFFFFFLL ? static_cast<int>(causal_m) : 0;
   if (n <= kTopkRegMax) {
     return topk_reg_launch(scores, rows, nn, ld, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, causal_start,
-                           0, nn, 1, st);
+                           0, nn, 1, st, p0);
   }
   // Stage plan: segment counts until the candidate list fits one register pass.
   int plan_nseg[8], plan_seg[8], plan_n[9];
@@ -414,15 +417,20 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
       for (int64_t r0 = 0; r0 < rows && rc == DSV32_OK; r0 += batch) {
         const int64_t rb = (rows - r0 < batch) ? rows - r0 : batch;
         // stage 0 reads the caller's rows (causal tail skipped), later stages the candidate lists
-        const float* in_v = scores + r0 * ld;
+        const float* in_v = scores ? scores + r0 * ld : nullptr;
         const int32_t* in_c = cand_idx ? cand_idx + r0 * cand_ld : nullptr;
         int64_t in_ld = ld, in_cld = cand_ld, off = idx_offset;
         int in_cm = cm;
         int64_t in_cs = causal_start;
         for (int sidx = 0; sidx < stages && rc == DSV32_OK; ++sidx) {
           const int b = sidx & 1;
+          dsv32::topk::RowParts pr = sidx == 0 ? p0 : no_parts;  // parts of this row batch
+          for (int j = 0; j < pr.n; ++j) {
+            pr.v[j] += r0 * pr.ld;
+            pr.id[j] += r0 * pr.ld;
+          }
           rc = topk_reg_launch(in_v, rb, plan_n[sidx], in_ld, in_c, in_cld, off, kk, bi[b], bv[b], in_cm, in_cs, r0,
-                               plan_seg[sidx], plan_nseg[sidx], st);
+                               plan_seg[sidx], plan_nseg[sidx], st, pr);
           in_v = bv[b];
           in_c = bi[b];
           in_ld = in_cld = plan_n[sidx + 1];
@@ -440,6 +448,7 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
       return DSV32_OK;
     }
   }
+  if (parts) return DSV32_ERR_UNSUPPORTED;  // the long-row kernel reads plain rows only
   return launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rows), 1024, 0, st, "topk kernel launch", scores, ld, nn,
                 cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
 }
@@ -560,6 +569,61 @@ int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const flo
 int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
                int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
   return topk_impl(scores, rows, n, ld, cand_idx, cand_ld, idx_offset, k, out_idx, out_val, stream);
+}
+
+int dsv32_device_alloc(int64_t bytes, void** ptr) {
+  if (!ptr || bytes < 1) return DSV32_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  const cudaError_t e = cudaMalloc(ptr, static_cast<size_t>(bytes));
+  return e == cudaSuccess ? DSV32_OK : cuda_fail(e, "cudaMalloc");
+}
+
+int dsv32_device_free(void* ptr) {
+  if (!ptr) return DSV32_OK;
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? DSV32_OK : cuda_fail(e, "cudaFree");
+}
+
+int dsv32_ipc_export(const void* ptr, void* handle) {
+  if (!ptr || !handle) return DSV32_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == DSV32_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return DSV32_OK;
+}
+
+int dsv32_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return DSV32_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? DSV32_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int dsv32_ipc_close(void* ptr) {
+  if (!ptr) return DSV32_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? DSV32_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
+                     int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
+  if (!part_vals || !part_ids || nparts < 1 || nparts > dsv32::topk::kMaxParts) return DSV32_ERR_INVALID_ARG;
+  if (rows < 1 || part_len < 1 || part_ld < part_len || k < 1 || k > nparts * part_len) return DSV32_ERR_INVALID_ARG;
+  if (part_len % 16 != 0 || nparts * part_len > (1LL << 30)) return DSV32_ERR_UNSUPPORTED;
+  dsv32::topk::RowParts parts{};
+  for (int j = 0; j < nparts; ++j) {
+    if (!part_vals[j] || !part_ids[j]) return DSV32_ERR_INVALID_ARG;
+    parts.v[j] = part_vals[j];
+    parts.id[j] = part_ids[j];
+  }
+  parts.ld = part_ld;
+  parts.len = static_cast<int>(part_len);
+  parts.n = nparts;
+  return topk_impl(nullptr, rows, nparts * part_len, part_ld, nullptr, 0, 0, k, out_idx, out_val, stream, 0, 0, &parts);
 }
 
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,

@@ -211,6 +211,17 @@ DSV32_DEV void copy_out_staged(const int32_t* sidx, const float* sval, int32_t* 
   }
 }
 
+// A row given as the concatenation of n lists of len positions each (list j of row r at v[j] + r * ld,
+// its candidate ids at id[j] + r * ld): the per-rank top-k lists of a key-sharded selection, read in
+// place, possibly from other GPUs' memory. n == 0: rows are plain (vals / cand_idx addressing).
+constexpr int kMaxParts = 16;
+struct RowParts {
+  const float* v[kMaxParts];
+  const int32_t* id[kMaxParts];
+  long long ld;
+  int len, n;
+};
+
 // Positions past n hold key 0 (below every real key except the all-ones negative NaN): they never
 // count as above -inf, never reach a histogram while the floor is above -inf, and never equal a
 // threshold >= the -inf key. Only the negative-NaN path (threshold below -inf) checks positions.
@@ -219,6 +230,8 @@ DSV32_DEV void copy_out_staged(const int32_t* sidx, const float* sval, int32_t* 
 // [seg0, seg0 + seg_len) of input row r' / nseg); nseg = 1, seg_len = n_total is the plain top-k.
 // Each segment's list is written to out row r' (k entries); the nseg lists of an input row are
 // contiguous, in segment order, so they form that row's candidate list for a merge pass.
+// With parts.n > 0 the row is the concatenation of the parts (parts.len a multiple of ITEMS, so the
+// ITEMS positions of a thread lie in one part) and candidate ids come from the parts.
 // Six 256-thread or three 512-thread CTAs per SM (40 registers, some spilled to L1): the barriers
 // between the selection phases are hidden by the other CTAs (4096 x 4096: 57.4 -> 53.1 us against
 // four 256-thread CTAs; 2048 x 131072 staged: 1593 -> 1461 us against two 512-thread CTAs).
@@ -228,7 +241,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
                                                            long long idx_offset, int k, int32_t* __restrict__ out_idx,
                                                            float* __restrict__ out_val, int causal_m,
                                                            long long causal_start, long long causal_row0,
-                                                           int seg_len, int nseg) {
+                                                           int seg_len, int nseg,
+                                                           const __grid_constant__ RowParts parts) {
   constexpr int W = THREADS / 32;
   static_assert(ITEMS <= 32, "per-thread selection masks are 32-bit");
   __shared__ RegShared<THREADS> sh;
@@ -239,20 +253,35 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   const long long row = out_row / nseg;
   const int seg0 = static_cast<int>(out_row % nseg) * seg_len;
   const int n = min(seg_len, n_total - seg0);
-  const float* v = vals + row * ld + seg0;
   const int valid = max(0, min(n, row_valid(row + causal_row0, n_total, causal_m, causal_start) - seg0));
   const int pos0 = tid * ITEMS;
+  // This thread's ITEMS positions: their scores and (merge passes) candidate ids. The ids are only
+  // needed at the end; the lambda recomputes their address there instead of holding it.
+  auto thread_part = [&]() { return min((seg0 + min(pos0, max(n - 1, 0))) / max(parts.len, 1), parts.n - 1); };
+  auto thread_ids = [&]() -> const int32_t* {
+    if (parts.n > 0) {
+      const int pj = thread_part();
+      return parts.id[pj] + row * parts.ld + (seg0 + pos0 - pj * parts.len);
+    }
+    return cand_idx ? cand_idx + row * cand_ld + seg0 + pos0 : nullptr;
+  };
+  const float* tv;
+  if (parts.n > 0) {
+    const int pj = thread_part();
+    tv = parts.v[pj] + row * parts.ld + (seg0 + pos0 - pj * parts.len);
+  } else {
+    tv = vals + row * ld + seg0 + pos0;
+  }
   pdl_wait();
   pdl_launch_dependents();
   for (int i = tid; i < kRegBins; i += THREADS) sh.u.hist[i] = 0;  // first radix pass
   uint32_t key[ITEMS];
   // Each thread owns ITEMS consecutive positions (position order = thread order). Positions in
   // [valid, n) are -inf without a read.
-  if ((ld & 3) == 0 && (seg0 & 3) == 0 && (reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && (ITEMS % 4) == 0 &&
-      pos0 + ITEMS <= valid) {
+  if ((reinterpret_cast<uintptr_t>(tv) & 15u) == 0 && (ITEMS % 4) == 0 && pos0 + ITEMS <= valid) {
 #pragma unroll
     for (int i = 0; i < ITEMS; i += 4) {
-      const float4 f = __ldg(reinterpret_cast<const float4*>(v + pos0 + i));
+      const float4 f = __ldg(reinterpret_cast<const float4*>(tv + i));
       key[i] = fkey(f.x);
       key[i + 1] = fkey(f.y);
       key[i + 2] = fkey(f.z);
@@ -261,7 +290,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   } else {
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i)
-      key[i] = (pos0 + i < valid) ? fkey(__ldg(v + pos0 + i)) : (pos0 + i < n ? kNegInfKey : 0u);
+      key[i] = (pos0 + i < valid) ? fkey(__ldg(tv + i)) : (pos0 + i < n ? kNegInfKey : 0u);
   }
   // 0. A row with at most k visible positions (a causal row that sees <= k keys) selects exactly its
   //    first k positions: every visible value is above the masked -inf tail, and the tail's ties go
@@ -273,12 +302,22 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
     for (int i = 0; i < ITEMS; ++i) neg_nan |= (pos0 + i < valid) && key[i] < kNegInfKey;
     if (!__syncthreads_or(neg_nan)) {  // (the barrier also orders the histogram clear above)
       // Output j is position j: a coalesced copy (the visible scores are re-read from L1 / L2).
-      const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
       int32_t* oi = out_idx + out_row * k;
       float* ov = out_val + out_row * k;
-      for (int j = tid; j < k; j += THREADS) {
-        oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
-        ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
+      if (parts.n > 0) {
+        for (int j = tid; j < k; j += THREADS) {
+          const int pj = (seg0 + j) / parts.len;
+          const long long off = row * parts.ld + (seg0 + j - pj * parts.len);
+          oi[j] = parts.id[pj][off];
+          ov[j] = j < valid ? __ldg(parts.v[pj] + off) : -INFINITY;
+        }
+      } else {
+        const float* v = vals + row * ld + seg0;
+        const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
+        for (int j = tid; j < k; j += THREADS) {
+          oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
+          ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
+        }
       }
       return;
     }
@@ -424,13 +463,13 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
       const bool staged = k <= kStageMax;
       int32_t* si = staged ? sh.u.out.idx : oi;
       float* sv = staged ? sh.u.out.val : ov;
-      if (cand_idx) {
-        const int32_t* cand_row = cand_idx + row * cand_ld + seg0;
+      if (cand_idx || parts.n > 0) {
+        const int32_t* ti = thread_ids();
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
           if (smask & (1u << i)) {
             const int slot = o + __popc(smask & ((1u << i) - 1u));
-            si[slot] = cand_row[pos0 + i];
+            si[slot] = ti[i];
             sv[slot] = fkey_inv(key[i]);
           }
         }
@@ -628,16 +667,16 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   while (__popc(emask) > take) emask &= ~(0x80000000u >> __clz(emask));  // drop the highest
   const uint32_t smask = gmask | emask;
   const int o = (packed >> 16) + min(eq_before, krem);
-  const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
   int32_t* oi = out_idx + out_row * k;
   float* ov = out_val + out_row * k;
   const bool staged = k <= kStageMax;
+  const int32_t* ti = thread_ids();
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     if (smask & (1u << i)) {
       const int pos = pos0 + i;
       const int slot = o + __popc(smask & ((1u << i) - 1u));
-      const int32_t id = cand_row ? cand_row[pos] : static_cast<int32_t>(pos + seg0 + idx_offset);
+      const int32_t id = ti ? ti[i] : static_cast<int32_t>(pos + seg0 + idx_offset);
       const float x = fkey_inv(key[i]);
       if (staged) {
         sh.u.out.idx[slot] = id;

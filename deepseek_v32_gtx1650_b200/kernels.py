@@ -10,6 +10,8 @@ path. Calling with CPU tensors raises, as the reference's Triton launch would.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -176,6 +178,39 @@ def select_topk(scores: torch.Tensor, k: int, idx_offset: int = 0, cand_idx: tor
     return idx, vals
 
 
+def _ptr_array(ptrs):
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    return ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), arr
+
+
+def topk_parts_raw(val_ptrs, id_ptrs, rows: int, part_ld: int, part_len: int, k: int, device: torch.device):
+    """Top-k over rows that are the concatenation of len(val_ptrs) lists given as raw device
+    addresses (list j of row r at val_ptrs[j] + 4 * r * part_ld, ids likewise), which may be other
+    GPUs' memory mapped with CUDA IPC. Returns (idx int32 [rows, k], vals fp32 [rows, k])."""
+    idx = torch.empty(rows, k, device=device, dtype=torch.int32)
+    vals = torch.empty(rows, k, device=device, dtype=torch.float32)
+    pv, keep_v = _ptr_array(val_ptrs)
+    pi, keep_i = _ptr_array(id_ptrs)
+    with _OnDevice(idx):
+        _lib.check(_lib.load().dsv32_topk_parts(pv, pi, len(val_ptrs), rows, part_ld, part_len, k, idx.data_ptr(),
+                                                vals.data_ptr(), _stream(idx)), "select_topk_parts")
+    return idx, vals
+
+
+def select_topk_parts(vals_list, idx_list, k: int):
+    """Top-k of rows given as lists: row r of the concatenation of vals_list[j][r] (each [rows, L]
+    fp32, L % 16 == 0) with candidate ids idx_list[j][r] (int32). The lists are read in place (no
+    concatenation copy); selection and ties as select_topk. Returns (idx int32 [rows, k], vals)."""
+    assert len(vals_list) == len(idx_list) and 1 <= len(vals_list) <= 16
+    rows, L = vals_list[0].shape
+    for v, i in zip(vals_list, idx_list):
+        assert v.dtype == torch.float32 and i.dtype == torch.int32 and v.is_contiguous() and i.is_contiguous()
+        assert v.shape == (rows, L) and i.shape == (rows, L) and v.device == vals_list[0].device
+    _require_cuda(*vals_list, *idx_list)
+    return topk_parts_raw([v.data_ptr() for v in vals_list], [i.data_ptr() for i in idx_list], rows, L, L, k,
+                          vals_list[0].device)
+
+
 def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_scores=True, key_offset=0):
     """Indexer scores + per-query top-k in one call (the step bench_indexer_e2e.py:54-57,72-77 runs).
 
@@ -197,6 +232,22 @@ def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_score
                                                  topk, int(key_offset), idx.data_ptr(), vals.data_ptr(), s),
                        "int8_index_topk")
     return (scores, idx, vals) if return_scores else (idx, vals)
+
+
+def int8_index_topk_into(q, w, k, k_s, out_idx_ptr: int, out_val_ptr: int, topk=2048, causal=False, start=0,
+                         key_offset=0):
+    """int8_index_topk writing the selection to raw device addresses ([b * m, topk] int32 ids and
+    fp32 values, e.g. a buffer other GPUs map); the scores go to a temporary."""
+    B, M, H, D, Nk = _index_checks(q, w, k, k_s)
+    assert 1 <= topk <= Nk, "topk must be in [1, n]"
+    _require_cuda(q, w, k, k_s)
+    scores = torch.empty(B, M, Nk, device=q.device, dtype=torch.float32)
+    if B and M:
+        with _OnDevice(q):
+            _lib.check(_lib.load().dsv32_int8_index_topk(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
+                                                         scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)),
+                                                         int(start), topk, int(key_offset), out_idx_ptr,
+                                                         out_val_ptr, _stream(q)), "int8_index_topk")
 
 
 def rotate_quant(x: torch.Tensor, rotate: bool = True):

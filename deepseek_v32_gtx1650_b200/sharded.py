@@ -22,9 +22,13 @@ hot path admits.
 """
 from __future__ import annotations
 
+import atexit
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from . import kernels as K
 
 
@@ -96,6 +100,66 @@ def merge_candidates(idx: torch.Tensor, vals: torch.Tensor, topk: int, group=Non
     return out_i, out_b.view(torch.float32)
 
 
+class PeerLists:
+    """This rank's top-k lists of `rows` rows (ids [rows, k] int32, then values [rows, k] fp32, in one
+    cudaMalloc allocation) and every peer's, mapped into this process with CUDA IPC, so the merge
+    kernel reads the other ranks' lists in place over NVLink. Built once per (rows, k, device, group)
+    by a collective (all ranks construct it together); released at exit."""
+
+    _cache: dict = {}
+
+    def __init__(self, rows: int, k: int, device: torch.device, group=None):
+        lib = _lib.load()
+        self.rows, self.k, self.world, self.rank = rows, k, dist.get_world_size(group), dist.get_rank(group)
+        with torch.cuda.device(device):
+            base = ctypes.c_void_p()
+            _lib.check(lib.dsv32_device_alloc(rows * k * 8, ctypes.byref(base)), "PeerLists alloc")
+            handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+            _lib.check(lib.dsv32_ipc_export(base, handle), "PeerLists export")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            self.bases, self.opened = [], []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.bases.append(base.value)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.check(lib.dsv32_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(peer)),
+                           "PeerLists open")
+                self.bases.append(peer.value)
+                self.opened.append(peer.value)
+        self.own = base.value
+        self.flag = torch.zeros(1, dtype=torch.int32, device=device)
+        atexit.register(self.close)
+
+    def ids_ptr(self, r: int, row0: int = 0) -> int:
+        return self.bases[r] + 4 * row0 * self.k
+
+    def vals_ptr(self, r: int, row0: int = 0) -> int:
+        return self.bases[r] + 4 * (self.rows + row0) * self.k
+
+    def close(self):
+        lib = _lib.load()
+        for p in self.opened:
+            lib.dsv32_ipc_close(ctypes.c_void_p(p))
+        self.opened = []
+        if self.own:
+            lib.dsv32_device_free(ctypes.c_void_p(self.own))
+            self.own = 0
+
+    @classmethod
+    def get(cls, rows: int, k: int, device: torch.device, group=None):
+        key = (rows, k, device.index, id(group))
+        if key not in cls._cache:
+            cls._cache[key] = cls(rows, k, device, group)
+        return cls._cache[key]
+
+
+def _p2p_usable(rows: int, k: int, world: int, device: torch.device, group=None) -> bool:
+    return (device.type == "cuda" and dist.get_backend(group) == "nccl" and 1 < world <= 16 and rows % world == 0
+            and k % 16 == 0)
+
+
 def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, causal: bool = False,
                        start: int = 0, group=None):
     """Key-range sharded indexer + top-k. q [B, M, H, D], w [B, M, H] replicated; k_local [B, n_r, D],
@@ -103,11 +167,32 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     vals fp32 [B, M, topk]) on every rank, identical to the single-GPU int8_index_topk."""
     B, M = q.shape[:2]
     assert k_local.shape[1] >= topk, "each key shard must hold at least topk keys"
-    idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
-                                  start=local_causal_start(start, key_lo), return_scores=False,
-                                  key_offset=key_lo)
-    midx, mval = merge_candidates(idx.view(B * M, topk), vals.view(B * M, topk), topk, group)
-    return midx.view(B, M, topk), mval.view(B, M, topk)
+    world = dist.get_world_size(group)
+    rows = B * M
+    if not _p2p_usable(rows, topk, world, q.device, group):
+        idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
+                                      start=local_causal_start(start, key_lo), return_scores=False,
+                                      key_offset=key_lo)
+        midx, mval = merge_candidates(idx.view(rows, topk), vals.view(rows, topk), topk, group)
+        return midx.view(B, M, topk), mval.view(B, M, topk)
+    # Peer-memory exchange: the local selection writes straight into this rank's mapped buffer, a
+    # one-element all-reduce orders every rank's selection before any read, and the merge kernel
+    # reads this rank's row block of every rank's lists in place over NVLink.
+    ex = PeerLists.get(rows, topk, q.device, group)
+    K.int8_index_topk_into(q, w, k_local, k_s_local, ex.ids_ptr(ex.rank), ex.vals_ptr(ex.rank), topk=topk,
+                           causal=causal, start=local_causal_start(start, key_lo), key_offset=key_lo)
+    dist.all_reduce(ex.flag, group=group)
+    r = rows // world
+    r0 = ex.rank * r
+    mi, mv = K.topk_parts_raw([ex.vals_ptr(j, r0) for j in range(world)], [ex.ids_ptr(j, r0) for j in range(world)],
+                              r, topk, topk, topk, q.device)
+    # Merged row blocks to every rank. A rank passes this point only after every rank's merge kernel
+    # has run (they precede the all-gather on each stream), so the next call may overwrite the lists.
+    out_i = torch.empty(rows, topk, dtype=torch.int32, device=q.device)
+    out_b = torch.empty(rows, topk, dtype=torch.int32, device=q.device)
+    dist.all_gather_into_tensor(out_i, mi, group=group)
+    dist.all_gather_into_tensor(out_b, mv.view(torch.int32), group=group)
+    return out_i.view(B, M, topk), out_b.view(torch.float32).view(B, M, topk)
 
 
 def sharded_int8_gemm(a, a_s, b_local, b_s_local, out_dtype=torch.float32):

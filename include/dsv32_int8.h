@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define DSV32_ABI_VERSION 4
+#define DSV32_ABI_VERSION 5
 
 /* Status codes. */
 #define DSV32_OK 0
@@ -143,6 +143,28 @@ int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int
  * aligned. Per 128 x 128 block: ws = max(amax, 1e-4) / 127 (fp32 division), wq = clamp(rint(w / ws),
  * -127, 127). wq int8 [n, k], ws fp32 [n/128, k/128]. */
 int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t* wq, float* ws, void* stream);
+
+/* Merge of key-sharded selections (the exchange step of a key-range sharded indexer; the reference
+ * runs on one GPU and has no such step, its single-GPU selection is test_kernels.py:125): row r is
+ * the concatenation of nparts lists, list j at part_vals[j] + r * part_ld (part_len scores) with
+ * their global key ids at part_ids[j] + r * part_ld. Selects as dsv32_topk does (ties: lower
+ * position in the concatenation first) and writes the ids from the lists. The lists are read in
+ * place and may live in other GPUs' memory (dsv32_ipc_open). 1 <= nparts <= 16, part_len % 16 == 0,
+ * 1 <= k <= nparts * part_len. out_idx / out_val [rows, k]. */
+int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
+                     int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* stream);
+
+/* Device memory another process on the node can map: cudaMalloc on the current device (the pointer
+ * is the base of its allocation, as IPC export requires), and its release. */
+int dsv32_device_alloc(int64_t bytes, void** ptr);
+int dsv32_device_free(void* ptr);
+
+/* CUDA IPC of such an allocation: export writes its DSV32_IPC_HANDLE_BYTES-byte handle; open maps a
+ * handle exported by another process (peer access enabled on first use), close unmaps it. */
+#define DSV32_IPC_HANDLE_BYTES 64
+int dsv32_ipc_export(const void* ptr, void* handle);
+int dsv32_ipc_open(const void* handle, void** ptr);
+int dsv32_ipc_close(void* ptr);
 
 /* DSV32_ABI_VERSION of the loaded library. */
 int dsv32_abi_version(void);

@@ -38,7 +38,7 @@ def test_library_builds_and_exports_every_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.dsv32_abi_version() == 4
+    assert lib.dsv32_abi_version() == 5
     for code in range(6):
         assert lib.dsv32_status_string(code)
     assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")
@@ -73,3 +73,22 @@ def test_no_device_is_an_error_not_a_fallback():
     fake = ctypes.c_void_p(4096)
     st = lib.dsv32_act_quant(fake, 0, 4, 128, 0, fake, fake, None)
     assert st in (_lib.DSV32_ERR_CUDA, _lib.DSV32_ERR_NO_DEVICE)
+
+
+def test_topk_parts_and_ipc_validation_without_gpu():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    ptrs = (ctypes.c_void_p * 2)(4096, 8192)
+    P = ctypes.POINTER(ctypes.c_void_p)
+    parts = ctypes.cast(ptrs, P)
+    # no parts, too many parts, k larger than the concatenated row, lists not a multiple of 16 long
+    assert lib.dsv32_topk_parts(parts, parts, 0, 4, 64, 64, 8, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts(parts, parts, 17, 4, 64, 64, 8, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 64, 129, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 40, 8, fake, fake, None) == _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 32, 64, 8, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    # null arguments of the memory / IPC helpers
+    assert lib.dsv32_device_alloc(0, ctypes.byref(ctypes.c_void_p())) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_ipc_export(None, fake) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_device_free(None) == _lib.DSV32_OK and lib.dsv32_ipc_close(None) == _lib.DSV32_OK

@@ -1,5 +1,6 @@
-"""Sharded paths on 2 GPUs over NCCL (skipped with fewer GPUs): the key-range sharded indexer + top-k
-merge equals the single-GPU int8_index_topk exactly; the N-sharded GEMM gathers to the 1-GPU output."""
+"""Sharded paths on 2 GPUs (skipped with fewer GPUs): the key-range sharded indexer + top-k merge
+(peer-memory exchange through CUDA IPC when the rows split evenly, NCCL all-gather otherwise) equals
+the single-GPU int8_index_topk exactly; the N-sharded GEMM gathers to the 1-GPU output."""
 import os
 import socket
 
@@ -27,14 +28,20 @@ def _worker(rank, world, port, q):
         import deepseek_v32_gtx1650_b200 as D
         from deepseek_v32_gtx1650_b200 import sharded as S, workloads as W
         dev = torch.device("cuda", rank)
-        M, N, k, start = 256, 16384, 2048, 16384 - 256
-        q_, w, keys, ks = W.index_inputs(1, M, N, seed=11)
-        lo, hi = S.shard_range(N, world, rank)
-        idx, vals = S.sharded_index_topk(q_.to(dev), w.to(dev), keys[:, lo:hi].contiguous().to(dev),
-                                         ks[:, lo:hi].contiguous().to(dev), lo, topk=k, causal=True, start=start)
-        gi, gv = D.int8_index_topk(q_.to(dev), w.to(dev), keys.to(dev), ks.to(dev), topk=k, causal=True,
-                                   start=start, return_scores=False)
-        ok_index = torch.equal(idx, gi) and torch.equal(vals, gv)
+        N, k = 16384, 2048
+
+        def index_case(M, seed):
+            start = N - M
+            q_, w, keys, ks = W.index_inputs(1, M, N, seed=seed)
+            lo, hi = S.shard_range(N, world, rank)
+            idx, vals = S.sharded_index_topk(q_.to(dev), w.to(dev), keys[:, lo:hi].contiguous().to(dev),
+                                             ks[:, lo:hi].contiguous().to(dev), lo, topk=k, causal=True, start=start)
+            gi, gv = D.int8_index_topk(q_.to(dev), w.to(dev), keys.to(dev), ks.to(dev), topk=k, causal=True,
+                                       start=start, return_scores=False)
+            return torch.equal(idx, gi) and torch.equal(vals, gv)
+
+        # 256 rows: peer-memory exchange (twice: the mapped lists are reused), 255 rows: NCCL all-gather
+        ok_index = index_case(256, 11) and index_case(256, 12) and index_case(255, 13)
         a, a_s, b, b_s = W.gemm_inputs_uniform(256, 256 * world, 1024, seed=5)
         blo, bhi = S.shard_range(b.shape[0], world, rank)
         c_loc = S.sharded_int8_gemm(a.to(dev), a_s.to(dev), b[blo:bhi].contiguous().to(dev),

@@ -57,6 +57,28 @@ def test_merge_of_shard_topk_equals_global(shards):
     assert torch.equal(midx, gidx) and torch.equal(mval, gval)
 
 
+@pytest.mark.parametrize("shards,n,k,rows", [(2, 16384, 2048, 5), (4, 16384, 2048, 37), (8, 65536, 2048, 3),
+                                              (16, 65536, 2048, 2), (3, 192, 100, 9), (5, 640, 64, 4)])
+def test_merge_of_shard_lists_in_place_equals_global(shards, n, k, rows):
+    """select_topk_parts reads the per-shard lists where they lie (no concatenation): identical to the
+    merge of the concatenated lists and to the one-shot top-k, ties included (integer-valued scores),
+    including single-pass, staged (8 and 16 lists of 2048) and short-list cases."""
+    s = _scores(rows, n, True, seed=shards * 7 + k).to(DEV)
+    s[0, : n // shards] = float("-inf")  # one shard of one row entirely masked
+    step = n // shards
+    kk = min(k, step)
+    parts = [D.select_topk(s[:, r * step:(r + 1) * step].contiguous(), kk, idx_offset=r * step) for r in range(shards)]
+    midx, mval = D.select_topk_parts([p[1] for p in parts], [p[0] for p in parts], k)
+    cidx = torch.cat([p[0] for p in parts], -1).contiguous()
+    cval = torch.cat([p[1] for p in parts], -1).contiguous()
+    ridx, rval = D.select_topk(cval, k, cand_idx=cidx)
+    assert torch.equal(midx, ridx) and torch.equal(mval, rval)
+    if kk == k:
+        gidx, gval = D.select_topk(s, k)
+        assert torch.equal(midx, gidx) and torch.equal(mval, gval)
+    assert_no_device_error()
+
+
 def test_index_topk_prefill_4096_causal():
     """BASELINE config 4 end to end: scores + top-2048 per query, causal."""
     M = N = 4096

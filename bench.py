@@ -376,7 +376,7 @@ class IndexWorkload(Workload):
         else:  # long, keys sharded by range
             self.B, self.M, self.N, self.causal, self.start = 1, 4096, 131072, True, 131072 - 4096
         self.scaling = "strong" if kind == "long" else "weak"
-        self.graphable = not (kind == "long" and world > 1)  # NCCL all-gather stays eager
+        self.graphable = True  # multi-GPU steps too: their NCCL calls are captured with the kernels
         self.name = f"index_{kind}"
         self.metric = {"prefill": "indexer prefill ms @4096^2 causal (scores + top-2048)",
                        "decode": "indexer decode ms (4 x 32768, scores + top-2048)",
@@ -841,23 +841,26 @@ def run_ours(args):
     else:
         kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     window = "timed region"
-    if len(sampler.samples) < 5 and not args.profile:  # timed region too short for NVML: sample a soak of the same step
+    # timed region too short for NVML: sample a soak of the same step. Decided and sized identically on
+    # every rank (a step may hold collectives, which every rank must run the same number of times).
+    t = torch.tensor([ms, kern_ms, 1.0 if (len(sampler.samples) < 5 and not args.profile) else 0.0], device=dev,
+                     dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kern_ms, need_soak = float(t[0]), float(t[1]), bool(t[2] > 0)
+    if need_soak:
         window = "soak of the same step right after the timed region (timed region too short for NVML)"
+        reps = max(1, min(100000, int(600.0 / max(ms if graph is not None else ms / args.steps, 1e-3))))
         sampler.start()
-        t0 = time.time()
-        i = 0
-        while time.time() - t0 < 0.6:
+        for i in range(reps):
             if graph is not None:
                 graph.replay()
             else:
                 wl.step(i)
-                i += 1
-            torch.cuda.synchronize()
+            if i % 64 == 63:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
         sampler.stop()
-    t = torch.tensor([ms, kern_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, kern_ms = float(t[0]), float(t[1])
     ms_step = ms / args.steps
     value = wl.value(ms_step, world)
 
@@ -906,6 +909,8 @@ def run_ours(args):
             v, sample = wl.cpu_sample(args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(v, 4), "unit": wl.unit, "cores": cpu_threads(), "kind": "port",
                                     "sample": sample}
+    del graph, kgraph  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -104,31 +104,44 @@ class PeerLists:
     """This rank's top-k lists of `rows` rows (ids [rows, k] int32, then values [rows, k] fp32, in one
     cudaMalloc allocation) and every peer's, mapped into this process with CUDA IPC, so the merge
     kernel reads the other ranks' lists in place over NVLink. Built once per (rows, k, device, group)
-    by a collective (all ranks construct it together); released at exit."""
+    by a collective (all ranks construct it together); released at exit. `usable` is False on every
+    rank if any rank could not allocate, export or map (the caller then exchanges through NCCL)."""
 
     _cache: dict = {}
 
     def __init__(self, rows: int, k: int, device: torch.device, group=None):
         lib = _lib.load()
         self.rows, self.k, self.world, self.rank = rows, k, dist.get_world_size(group), dist.get_rank(group)
+        self.bases, self.opened, self.own = [], [], 0
+        ok = True
         with torch.cuda.device(device):
             base = ctypes.c_void_p()
-            _lib.check(lib.dsv32_device_alloc(rows * k * 8, ctypes.byref(base)), "PeerLists alloc")
             handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
-            _lib.check(lib.dsv32_ipc_export(base, handle), "PeerLists export")
+            if lib.dsv32_device_alloc(rows * k * 8, ctypes.byref(base)) == _lib.DSV32_OK:
+                self.own = base.value
+                ok = lib.dsv32_ipc_export(base, handle) == _lib.DSV32_OK
+            else:
+                ok = False
             handles = [None] * self.world
-            dist.all_gather_object(handles, handle.raw, group=group)
-            self.bases, self.opened = [], []
+            dist.all_gather_object(handles, handle.raw if ok else b"", group=group)
             for r, h in enumerate(handles):
                 if r == self.rank:
-                    self.bases.append(base.value)
+                    self.bases.append(self.own)
                     continue
                 peer = ctypes.c_void_p()
-                _lib.check(lib.dsv32_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(peer)),
-                           "PeerLists open")
-                self.bases.append(peer.value)
-                self.opened.append(peer.value)
-        self.own = base.value
+                if ok and h and lib.dsv32_ipc_open(ctypes.create_string_buffer(h, len(h)),
+                                                   ctypes.byref(peer)) == _lib.DSV32_OK:
+                    self.bases.append(peer.value)
+                    self.opened.append(peer.value)
+                else:
+                    ok = False
+                    self.bases.append(0)
+            # every rank takes the same exchange path: usable only if every mapping succeeded everywhere
+            t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+            self.usable = bool(t.item())
+        if not self.usable:
+            self.close()
         self.flag = torch.zeros(1, dtype=torch.int32, device=device)
         atexit.register(self.close)
 
@@ -179,6 +192,12 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     # one-element all-reduce orders every rank's selection before any read, and the merge kernel
     # reads this rank's row block of every rank's lists in place over NVLink.
     ex = PeerLists.get(rows, topk, q.device, group)
+    if not ex.usable:  # no peer mappings on this system (decided collectively): NCCL exchange
+        idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
+                                      start=local_causal_start(start, key_lo), return_scores=False,
+                                      key_offset=key_lo)
+        midx, mval = merge_candidates(idx.view(rows, topk), vals.view(rows, topk), topk, group)
+        return midx.view(B, M, topk), mval.view(B, M, topk)
     K.int8_index_topk_into(q, w, k_local, k_s_local, ex.ids_ptr(ex.rank), ex.vals_ptr(ex.rank), topk=topk,
                            causal=causal, start=local_causal_start(start, key_lo), key_offset=key_lo)
     dist.all_reduce(ex.flag, group=group)

@@ -54,6 +54,19 @@ def test_cpu_tensors_are_refused():
         D.int8_gemm(a, torch.zeros(4, 1), torch.zeros(128, 128, dtype=torch.int8), torch.zeros(1, 1))
 
 
+def test_select_topk_parts_checks():
+    v = [torch.zeros(3, 32), torch.zeros(3, 32)]
+    i = [torch.zeros(3, 32, dtype=torch.int32), torch.zeros(3, 32, dtype=torch.int32)]
+    with pytest.raises(AssertionError):  # lists of different shapes
+        D.select_topk_parts([v[0], torch.zeros(3, 48)], i, 8)
+    with pytest.raises(AssertionError):  # ids must be int32
+        D.select_topk_parts(v, [i[0], i[1].long()], 8)
+    with pytest.raises(AssertionError):  # at most 16 lists
+        D.select_topk_parts(v * 9, i * 9, 8)
+    with pytest.raises(RuntimeError):  # no CPU path
+        D.select_topk_parts(v, i, 8)
+
+
 def test_kmajor_roundtrip_cpu():
     t = torch.randint(-127, 128, (37, 256), dtype=torch.int8)
     assert torch.equal(D.unkmajor(D.kmajor(t)), t)

@@ -7,15 +7,15 @@ Only the two paths that shard naturally are partitioned:
   optionally all-gathers the column slices into the full [M, N] output.
 - The indexer by key range: rank r owns keys [lo, hi) of the key cache (lo a multiple of 128).
   It scores every query against its keys with the causal limit shifted by -lo and selects its
-  local top-k (global key ids = lo + position). The lists are then merged by query row: an
-  all-to-all over NVLink hands rank r the lists of its 1/world of the rows from every rank, it
-  merges those rows' world * k candidates with the same top-k kernel, and an all-gather of the
-  merged rows gives every rank the whole result. Each rank moves about 2 * rows * k * 8 bytes and
-  merges rows / world rows, whatever the world size (gathering every list to every rank moves
-  world times that and merges every row everywhere; it remains the path when the rows do not
-  split evenly). Local lists are position-ordered and concatenated in rank order, so ties resolve
-  to the lowest global key id exactly as in the single-GPU selection; the merged result is
-  identical to it.
+  local top-k (global key ids = lo + position). The lists are then merged by query row: each
+  rank's selection lands in a buffer every rank maps with CUDA IPC (PeerLists), a one-element
+  all-reduce orders all selections before any read, rank r merges its rows / world rows with the
+  top-k kernel reading every rank's lists in place over NVLink (dsv32_topk_parts), and an
+  all-gather of the merged rows gives every rank the whole result. When the rows do not split
+  evenly or peer mappings are unavailable, merge_candidates does the exchange with NCCL
+  all-to-alls (or an all-gather). Local lists are position-ordered and concatenated in rank order,
+  so ties resolve to the lowest global key id exactly as in the single-GPU selection; the merged
+  result is identical to it.
 
 The reference has no multi-GPU code (single GTX 1650); these are the two exchange patterns its
 hot path admits.
@@ -182,24 +182,18 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     assert k_local.shape[1] >= topk, "each key shard must hold at least topk keys"
     world = dist.get_world_size(group)
     rows = B * M
-    if not _p2p_usable(rows, topk, world, q.device, group):
-        idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
-                                      start=local_causal_start(start, key_lo), return_scores=False,
-                                      key_offset=key_lo)
+    lstart = local_causal_start(start, key_lo)
+    ex = PeerLists.get(rows, topk, q.device, group) if _p2p_usable(rows, topk, world, q.device, group) else None
+    if ex is None or not ex.usable:  # (usable is decided collectively: every rank takes the same path)
+        idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal, start=lstart,
+                                      return_scores=False, key_offset=key_lo)
         midx, mval = merge_candidates(idx.view(rows, topk), vals.view(rows, topk), topk, group)
         return midx.view(B, M, topk), mval.view(B, M, topk)
     # Peer-memory exchange: the local selection writes straight into this rank's mapped buffer, a
     # one-element all-reduce orders every rank's selection before any read, and the merge kernel
     # reads this rank's row block of every rank's lists in place over NVLink.
-    ex = PeerLists.get(rows, topk, q.device, group)
-    if not ex.usable:  # no peer mappings on this system (decided collectively): NCCL exchange
-        idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal,
-                                      start=local_causal_start(start, key_lo), return_scores=False,
-                                      key_offset=key_lo)
-        midx, mval = merge_candidates(idx.view(rows, topk), vals.view(rows, topk), topk, group)
-        return midx.view(B, M, topk), mval.view(B, M, topk)
     K.int8_index_topk_into(q, w, k_local, k_s_local, ex.ids_ptr(ex.rank), ex.vals_ptr(ex.rank), topk=topk,
-                           causal=causal, start=local_causal_start(start, key_lo), key_offset=key_lo)
+                           causal=causal, start=lstart, key_offset=key_lo)
     dist.all_reduce(ex.flag, group=group)
     r = rows // world
     r0 = ex.rank * r

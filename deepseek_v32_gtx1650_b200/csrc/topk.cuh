@@ -8,6 +8,10 @@
 // so "lower position" is "lower global key index", and the merge of per-shard top-k lists
 // reproduces the single-GPU selection exactly.
 //
+// NaN: keys follow the bit pattern, so a NaN with the sign bit clear (every NaN the indexer or any
+// fp32 arithmetic produces) ranks above +inf, as in torch.topk; a NaN with the sign bit set, which
+// only a caller's own scores can hold, ranks below -inf (torch.topk ranks every NaN first).
+//
 // Algorithm (radix select on order-preserving uint32 keys; larger float -> larger key):
 //  1. Block reductions give the number of finite values and the min / max finite key. Masked
 //     (-inf) scores never enter a histogram: when at most k values are finite, the threshold is

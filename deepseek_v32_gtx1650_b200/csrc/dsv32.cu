@@ -388,7 +388,10 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   while (plan_n[stages] > kTopkRegMax) {
     const int cur = plan_n[stages];
     const int nseg = (cur + kTopkRegMax - 1) / kTopkRegMax;
-    const int seg = ((cur + nseg - 1) / nseg + 3) & ~3;
+    // segment starts on 16-position boundaries when the first pass reads lists (a thread's 16
+    // positions must not straddle two lists), else on 4-position (16-byte) boundaries
+    const int align = (parts && stages == 0) ? 15 : 3;
+    const int seg = ((cur + nseg - 1) / nseg + align) & ~align;
     if (stages == 8 || cur - (nseg - 1) * seg < kk || static_cast<int64_t>(nseg) * kk >= cur) {
       staged_ok = false;
       break;

@@ -58,11 +58,13 @@ def test_merge_of_shard_topk_equals_global(shards):
 
 
 @pytest.mark.parametrize("shards,n,k,rows", [(2, 16384, 2048, 5), (4, 16384, 2048, 37), (8, 65536, 2048, 3),
-                                              (16, 65536, 2048, 2), (3, 192, 100, 9), (5, 640, 64, 4)])
+                                              (16, 65536, 2048, 2), (3, 192, 100, 9), (5, 640, 64, 4),
+                                              (5, 10000, 2000, 3)])
 def test_merge_of_shard_lists_in_place_equals_global(shards, n, k, rows):
     """select_topk_parts reads the per-shard lists where they lie (no concatenation): identical to the
     merge of the concatenated lists and to the one-shot top-k, ties included (integer-valued scores),
-    including single-pass, staged (8 and 16 lists of 2048) and short-list cases."""
+    including single-pass, staged (8 and 16 lists of 2048; 5 lists of 2000, whose stage segments
+    must start on list-aligned 16-position boundaries) and short-list cases."""
     s = _scores(rows, n, True, seed=shards * 7 + k).to(DEV)
     s[0, : n // shards] = float("-inf")  # one shard of one row entirely masked
     step = n // shards

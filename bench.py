@@ -6,17 +6,23 @@
 Default workload: block-scaled int8_gemm "expert up", M=4096 K=7168 N=2048,
 bf16 out, per GPU. With N GPUs (torchrun, one rank per GPU) the weight is sharded by N: global
 N = 2048 * world, each rank computes its own 2048 columns (weak scaling, no data-path collective).
-Other workloads: gemm_down (K=2048 N=7168, --m), act_quant (fp32/bf16 [2048, 7168]),
-index_prefill (4096 x 4096 causal, scores + top-2048), index_decode (4 x 32768 + top-2048),
-index_long (4096 queries x 131072 keys causal, keys sharded by range, per-shard top-2048 merged by
-query row after an NCCL all-to-all, merged rows all-gathered).
+The default line also carries a `secondary` list measured the same way: at one GPU the rest of
+BASELINE's metric (indexer prefill step 4096^2 causal with top-2048, act_quant fp32 and bf16) and
+the long-context indexer; at N GPUs the long-context indexer (4096 queries x 131072 keys, keys
+sharded by range over the ranks, strong scaling) with its per-stage times and a parity check of the
+merged selection against a one-GPU selection over all keys.
+Other workloads (--workload): gemm_down (K=2048 N=7168, --m), act_quant (--aq-dtype), index_prefill,
+index_decode (4 x 32768), index_long, index_step (rotate + quantise q/k, scores, top-2048),
+rotate_quant, weight_quant.
 
-Timing: W untimed warm-up steps, then K steps between a barrier + synchronize on both sides,
-CUDA events on the launching stream, max over ranks. Inputs rotate over enough copies to exceed
-the 126 MB L2 between reuses. `value` = units of all ranks / max time. `e2e` repeats the step
-through the public API with pinned-host inputs copied in and the result copied out inside the
-timed region. `roofline` uses the dominant kernel's per-launch CUDA-event time.
-`--impl reference` times the CPU oracle port of reference.py (the reference's own CPU path) on a
+Timing: W untimed warm-up steps, then K steps captured in one CUDA graph (multi-GPU steps with their
+NCCL calls) and replayed between CUDA events on the launching stream, a barrier + synchronize on
+both sides, max over ranks. Inputs rotate over enough copies to exceed 2 x the 126 MB L2 between
+reuses. `value` = units of all ranks / max time. `e2e` repeats the step through the public API with
+pinned-host inputs copied in and the result copied out inside the timed region. `roofline` uses the
+dominant kernel's per-launch CUDA-event time.
+`--impl reference` times the reference's own CPU paths (PyTorch on the host cores: reference.py's
+act_quant_torch, gemm_dequant_fp32, index_torch_int8, restated in oracle/reference_torch.py) on a
 bounded sample of the same workload, on rank 0 only.
 """
 from __future__ import annotations
@@ -119,13 +125,28 @@ class ClockSampler:
                 "reasons": sorted(names), "samples": len(self.samples), "window": window}
 
 
-def cpu_threads():
+def cpu_setup():
+    """All host cores for the CPU baselines; returns the thread count actually used."""
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
     except Exception:
-        return os.cpu_count() or 1
+        pass
+    return torch.get_num_threads()
+
+
+def timed_loop(fn, seconds):
+    """Runs fn until `seconds` have passed (at least once); returns (seconds per call, calls)."""
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        fn()
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    return (time.perf_counter() - t0) / n, n
 
 
 # ------------------------------------------------------------------------------------------ workloads
@@ -138,9 +159,25 @@ class Workload:
     scaling = "weak"
     launches_per_step = 1
     graphable = True  # the timed steps can be captured in one CUDA graph
+    R = 1
+    l2_note = ""
 
-    def value_from(self, units_per_step_all_ranks, ms_per_step):
-        raise NotImplementedError
+    def set_rotation(self, set_bytes: int, what: str):
+        """Copies of the per-step inputs so that consecutive steps never hit the same data in L2."""
+        self.R = max(2, math.ceil(2 * L2_BYTES / set_bytes)) if set_bytes < 2 * L2_BYTES else 1
+        self.l2_note = f"{self.R} rotating {what} x {set_bytes / 1e6:.1f} MB (> 2 x 126 MB L2)"
+
+    def config_full(self):
+        return dict(self.config(), l2=self.l2_note)
+
+    def extra(self, dev, ms_step, kern_ms):
+        """Workload-specific keys measured after the timed region (same collectives on every rank)."""
+        return {}
+
+    def release(self):
+        for a in ("sets", "scores", "din2", "hin", "hout", "cache", "dev_in", "_qq", "_w2"):
+            if hasattr(self, a):
+                delattr(self, a)
 
     # e2e through the public API: pinned host inputs -> device, the call, outputs -> pinned host.
     def e2e_buffers(self, dev, hin, hout):
@@ -157,9 +194,6 @@ class Workload:
     def e2e_d2h(self, outs):
         for h, d in zip(self.hout, outs):
             h.copy_(d, non_blocking=True)
-
-    def e2e_run(self, din):
-        raise NotImplementedError
 
 
 def e2e_pipeline(wl, steps):
@@ -204,6 +238,9 @@ class GemmWorkload(Workload):
         self.unit = "TOP/s"
         self.seed = seed
         self.ops = 2.0 * M * N * K
+        ob = 2 if out == "bf16" else 4
+        self.bytes_alg = M * K + N * K + M * (K // 128) * 4 + (N // 128) * (K // 128) * 4 + M * N * ob
+        self.set_rotation(self.bytes_alg, "input sets")
 
     def config(self):
         return {"workload": f"int8_gemm {self.name} M={self.M} K={self.K} N={self.N} per GPU "
@@ -211,41 +248,29 @@ class GemmWorkload(Workload):
                 "M": self.M, "K": self.K, "N_per_gpu": self.N, "out_dtype": self.out,
                 "parallelism": f"N-shard x{self.world}"}
 
-    def prepare(self, dev):
-        import deepseek_v32_gtx1650_b200 as D
+    def host_inputs(self):
         from deepseek_v32_gtx1650_b200 import workloads as W
-        self.D = D
         x, B, b_s = W.gemm_inputs(self.M, self.N * self.world, self.K, seed=self.seed)
         lo, hi = self.rank * self.N, (self.rank + 1) * self.N
-        B, b_s = B[lo:hi].contiguous(), b_s[lo // 128:hi // 128].contiguous()
+        return x, B[lo:hi].contiguous(), b_s[lo // 128:hi // 128].contiguous()
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        self.D = D
+        x, B, b_s = self.host = self.host_inputs()
         A, a_s = D.act_quant(x.to(dev))
-        self.host = (x, B, b_s)
         self.odt = torch.bfloat16 if self.out == "bf16" else torch.float32
-        set_bytes = A.numel() + a_s.numel() * 4 + B.numel() + b_s.numel() * 4 + self.M * self.N * (2 if self.out == "bf16" else 4)
-        self.R = max(2, math.ceil(2 * L2_BYTES / set_bytes))
-        self.sets = []
-        for r in range(self.R):
-            self.sets.append((A.clone(), a_s.clone(), B.to(dev), b_s.to(dev),
-                              torch.empty(self.M, self.N, device=dev, dtype=self.odt)))
-        self.l2_note = f"{self.R} rotating input sets x {set_bytes / 1e6:.1f} MB (> 2 x 126 MB L2)"
-        self.bytes_alg = A.numel() + B.numel() + a_s.numel() * 4 + b_s.numel() * 4 + self.M * self.N * (2 if self.out == "bf16" else 4)
+        self.sets = [(A.clone(), a_s.clone(), B.to(dev), b_s.to(dev),
+                      torch.empty(self.M, self.N, device=dev, dtype=self.odt)) for _ in range(self.R)]
 
     def step(self, i, ev=None):
         A, a_s, B, b_s, C = self.sets[i % self.R]
-        if ev:
-            ev[0].record()
         # public API, writes into a fresh tensor; C is kept only to hold the set's footprint
         self.D.int8_gemm(A, a_s, B, b_s, out_dtype=self.odt)
-        if ev:
-            ev[1].record()
-
-    def units(self):
-        return self.ops
 
     def value(self, ms, world):
         return self.ops * world / (ms * 1e-3) / 1e12
 
-    # e2e: host pinned inputs -> device, public API call, result -> pinned host
     def e2e_prepare(self, dev):
         A, a_s, B, b_s, _ = self.sets[0]
         self.e2e_buffers(dev, tuple(t.cpu().pin_memory() for t in (A, a_s, B, b_s)),
@@ -259,61 +284,62 @@ class GemmWorkload(Workload):
         peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
         ach = self.ops / (kernel_ms * 1e-3) / 1e12
         return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
-                "frac": round(ach / peak, 4), "traffic": traffic.get(self.traffic_key()),
+                "frac": round(ach / peak, 4), "traffic": traffic.get(f"int8_gemm_{self.name}"),
                 "peak_note": f"dense INT8 = 2 x {src} cuBLAS bf16 burst ({peaks.get('bf16_tflops')} TF/s); "
                              f"nominal 4500 TOP/s",
                 "algorithmic_bytes": self.bytes_alg, "ops_per_launch": self.ops}
 
-    def traffic_key(self):
-        return f"int8_gemm_{self.name}"
-
     def cpu_sample(self, seconds):
+        """The reference's float path on the host (reference.py:43-48 gemm_dequant_fp32): activations
+        dequantised per block, one fp32 matmul against the weights dequantised once beforehand, on a
+        row sample. Also timed briefly: torch._int_mm without scales (reference.py:56-58) and the
+        float64 exact reference (reference.py:18-24)."""
+        from oracle import reference_torch as RT
         import oracle as O
-        x, B, b_s = self.host
-        rows = min(self.M, 128)
-        a, a_s = O.act_quant_ref(x[:rows].float().numpy())
-        Bn, bsn = B.numpy(), b_s.numpy()
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            O.int8_gemm_ref(a, a_s, Bn, bsn)
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = time.perf_counter() - t0
-        val = 2.0 * rows * self.N * self.K * n / dt / 1e12
-        return val, f"oracle int8_gemm_ref (float64 dequant + matmul, reference.py:18-24) on {rows} of {self.M} rows, {n} reps"
+        x, B, b_s = self.host if hasattr(self, "host") else self.host_inputs()
+        rows = min(self.M, 512)
+        A, a_s = RT.act_quant_torch(x[:rows])
+        b_deq = RT.dequant_weight(B, b_s)
+        dt, n = timed_loop(lambda: RT.gemm_dequant_fp32(A, a_s, b_deq), seconds)
+        value = 2.0 * rows * self.N * self.K / dt / 1e12
+        bT = B.T.contiguous()
+        dt_i, _ = timed_loop(lambda: RT.int_mm_unscaled(A, bT), min(seconds, 2.0))
+        r64 = min(rows, 64)
+        An, asn, Bn, bsn = A[:r64].numpy(), a_s[:r64].numpy(), B.numpy(), b_s.numpy()
+        dt_o, _ = timed_loop(lambda: O.int8_gemm_ref(An, asn, Bn, bsn), min(seconds, 2.0))
+        variants = {"gemm_dequant_fp32 (reference.py:43-48)": round(value, 4),
+                    "int_mm_unscaled (reference.py:56-58, no scales)": round(2.0 * rows * self.N * self.K / dt_i / 1e12, 4),
+                    "int8_gemm_ref float64 (reference.py:18-24)": round(2.0 * r64 * self.N * self.K / dt_o / 1e12, 4)}
+        return value, (f"torch on CPU: gemm_dequant_fp32 (reference.py:43-48) on {rows} of {self.M} rows against "
+                       f"the pre-dequantised weight, {n} reps"), variants
 
 
 class ActQuantWorkload(Workload):
     def __init__(self, M, N, dt, rank, world):
         self.M, self.N, self.dt = M, N, dt
         self.name = f"act_quant_{dt}"
-        self.metric = "act_quant GB/s"
+        self.metric = f"act_quant GB/s ({dt})"
         self.unit = "GB/s"
         self.dtype = "fp32->int8" if dt == "fp32" else "bf16->int8"
         self.tdt = torch.float32 if dt == "fp32" else torch.bfloat16
         self.bytes = M * N * (torch.tensor([], dtype=self.tdt).element_size() + 1) + M * (N // 128) * 4
+        self.set_rotation(self.bytes, "inputs")
 
     def config(self):
         return {"workload": f"act_quant {self.dt} [{self.M}, {self.N}] -> int8 + fp32 scales"}
 
+    def host_inputs(self):
+        from deepseek_v32_gtx1650_b200 import workloads as W
+        return W.act_quant_input(self.M, self.N).to(self.tdt)
+
     def prepare(self, dev):
         import deepseek_v32_gtx1650_b200 as D
-        from deepseek_v32_gtx1650_b200 import workloads as W
         self.D = D
-        x = W.act_quant_input(self.M, self.N).to(self.tdt)
-        self.host = x
-        self.R = max(2, math.ceil(2 * L2_BYTES / self.bytes))
-        self.sets = [x.to(dev) for _ in range(self.R)]
-        self.l2_note = f"{self.R} rotating inputs x {self.bytes / 1e6:.1f} MB"
+        self.host = self.host_inputs()
+        self.sets = [self.host.to(dev) for _ in range(self.R)]
 
     def step(self, i, ev=None):
-        if ev:
-            ev[0].record()
         self.D.act_quant(self.sets[i % self.R])
-        if ev:
-            ev[1].record()
 
     def value(self, ms, world):
         return self.bytes * world / (ms * 1e-3) / 1e9
@@ -334,24 +360,18 @@ class ActQuantWorkload(Workload):
                 "algorithmic_bytes": self.bytes}
 
     def cpu_sample(self, seconds):
-        import oracle as O
-        rows = min(self.M, 512)
-        x = self.host[:rows].float().numpy()
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            O.act_quant_ref(x)
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = time.perf_counter() - t0
-        b = rows * self.N * (self.tdt.itemsize + 1) + rows * (self.N // 128) * 4
-        return b * n / dt / 1e9, f"oracle act_quant_ref (reference.py:8-15) on {rows} of {self.M} rows, {n} reps"
+        """reference.py:38-40 act_quant_torch (eager PyTorch) on the whole input."""
+        from oracle import reference_torch as RT
+        x = self.host if hasattr(self, "host") else self.host_inputs()
+        dt, n = timed_loop(lambda: RT.act_quant_torch(x), seconds)
+        return self.bytes / dt / 1e9, (f"torch on CPU: act_quant_torch (reference.py:38-40) on the whole "
+                                       f"[{self.M}, {self.N}] {self.dt} input, {n} reps"), {}
 
 
 def topk_launches(rows, n, k, reg_max=8192, temp_bytes=256 << 20):
-    """Kernel launches of one library top-k call (mirrors topk_impl in csrc/dsv32.cu): one register
-    pass for rows up to 8192, else (segment stages + final merge) per row batch."""
+    """Kernel launches of one library top-k call (mirrors topk_impl in csrc/dsv32.cu with the
+    workspace dsv32_topk_workspace_bytes asks for): one register pass for rows up to 8192, else
+    (segment stages + final merge) per row batch."""
     if n <= reg_max:
         return 1
     plan = [n]
@@ -376,7 +396,6 @@ class IndexWorkload(Workload):
         else:  # long, keys sharded by range
             self.B, self.M, self.N, self.causal, self.start = 1, 4096, 131072, True, 131072 - 4096
         self.scaling = "strong" if kind == "long" else "weak"
-        self.graphable = True  # multi-GPU steps too: their NCCL calls are captured with the kernels
         self.name = f"index_{kind}"
         self.metric = {"prefill": "indexer prefill ms @4096^2 causal (scores + top-2048)",
                        "decode": "indexer decode ms (4 x 32768, scores + top-2048)",
@@ -390,14 +409,18 @@ class IndexWorkload(Workload):
         self.pairs = pairs * self.B
         self.ops = 2.0 * self.pairs * H * D
         self.ops_full = 2.0 * self.B * self.M * self.N * H * D
+        from deepseek_v32_gtx1650_b200 import sharded as S
+        self.lo, self.hi = S.shard_range(self.N, world, rank) if kind == "long" else (0, self.N)
+        nloc = self.hi - self.lo
         # our kernels per step: the indexer, the selection over this rank's keys, and for key-sharded
-        # runs the merge of the gathered candidate lists
+        # runs the merge of the ranks' lists (rows / world rows per rank when they split evenly)
         rows = self.B * self.M
-        nloc = (self.N + world - 1) // world if kind == "long" else self.N
         self.launches_per_step = 1 + topk_launches(rows, nloc, topk)
-        if kind == "long" and world > 1:  # merge: rows / world rows per rank when they split evenly
+        if kind == "long" and world > 1:
             mrows = rows // world if rows % world == 0 else rows
             self.launches_per_step += topk_launches(mrows, world * topk, topk)
+        set_bytes = self.B * self.M * H * D + self.B * self.M * H * 4 + self.B * nloc * (D + 4) + self.B * self.M * nloc * 4
+        self.set_rotation(set_bytes, "input sets")
 
     def config(self):
         return {"workload": f"lightning indexer {self.kind}: B={self.B} M={self.M} N={self.N} H=64 D=128 "
@@ -405,63 +428,44 @@ class IndexWorkload(Workload):
                 "visible_pairs": self.pairs,
                 "parallelism": f"key-range x{self.world}" if self.kind == "long" else f"replicas x{self.world}"}
 
+    def host_inputs(self):
+        from deepseek_v32_gtx1650_b200 import workloads as W
+        return W.index_inputs(self.B, self.M, self.N, seed=0)
+
     def prepare(self, dev):
         import deepseek_v32_gtx1650_b200 as D
-        from deepseek_v32_gtx1650_b200 import workloads as W, sharded as S
+        from deepseek_v32_gtx1650_b200 import sharded as S
         self.D, self.S = D, S
-        q, w, k, ks = W.index_inputs(self.B, self.M, self.N, seed=0)
-        self.host = (q, w, k, ks)
-        if self.kind == "long":
-            self.lo, self.hi = S.shard_range(self.N, self.world, self.rank)
-            k, ks = k[:, self.lo:self.hi].contiguous(), ks[:, self.lo:self.hi].contiguous()
-        else:
-            self.lo, self.hi = 0, self.N
-        nloc = self.hi - self.lo
-        set_bytes = q.numel() + w.numel() * 4 + k.numel() + ks.numel() * 4 + self.B * self.M * nloc * 4
-        self.R = max(1, math.ceil(2 * L2_BYTES / set_bytes)) if set_bytes < 2 * L2_BYTES else 1
-        self.sets = [(q.to(dev), w.to(dev), k.to(dev), ks.to(dev)) for _ in range(self.R)]
-        self.scores = torch.empty(self.B, self.M, nloc, device=dev)
-        self.l2_note = f"{self.R} rotating input sets x {set_bytes / 1e6:.1f} MB"
-        self.bytes_alg = set_bytes
+        q, w, k, ks = self.host = self.host_inputs()
+        kl, ksl = k[:, self.lo:self.hi].contiguous(), ks[:, self.lo:self.hi].contiguous()
+        self.sets = [(q.to(dev), w.to(dev), kl.to(dev), ksl.to(dev)) for _ in range(self.R)]
+
+    def _call(self, q, w, k, ks, return_scores, events=None):
+        if self.kind == "long" and self.world > 1:
+            return self.S.sharded_index_topk(q, w, k, ks, self.lo, self.topk, self.causal, self.start, events=events)
+        # scores + top-k through the fused entry point (the selection skips causal tails)
+        return self.D.int8_index_topk(q, w, k, ks, topk=self.topk, causal=self.causal, start=self.start - self.lo,
+                                      return_scores=return_scores, key_offset=self.lo)
 
     def step(self, i, ev=None, main_only=False):
         q, w, k, ks = self.sets[i % self.R]
-        D = self.D
         if main_only:
-            D.int8_index(q, w, k, ks, causal=self.causal, start=self.start - self.lo)
+            self.D.int8_index(q, w, k, ks, causal=self.causal, start=self.start - self.lo)
             return
-        if self.kind == "long" and self.world > 1:
-            if ev:
-                ev[0].record()
-            self.S.sharded_index_topk(q, w, k, ks, self.lo, self.topk, self.causal, self.start)
-            if ev:
-                ev[1].record()
-            return
-        if ev:
-            ev[0].record()
-        # scores + top-k through the fused entry point (the selection skips causal tails)
-        D.int8_index_topk(q, w, k, ks, topk=self.topk, causal=self.causal, start=self.start - self.lo,
-                          return_scores=True, key_offset=self.lo)
-        if ev:
-            ev[1].record()
+        self._call(q, w, k, ks, return_scores=self.kind != "long")
 
     def value(self, ms, world):
         return ms
 
     def e2e_prepare(self, dev):
-        q, w, k, ks = (t.pin_memory() for t in self.host)
-        if self.kind == "long":
-            k, ks = k[:, self.lo:self.hi].contiguous().pin_memory(), ks[:, self.lo:self.hi].contiguous().pin_memory()
-        self.e2e_buffers(dev, (q, w, k, ks),
+        q, w, k, ks = self.host
+        k, ks = k[:, self.lo:self.hi].contiguous(), ks[:, self.lo:self.hi].contiguous()
+        self.e2e_buffers(dev, tuple(t.pin_memory() for t in (q, w, k, ks)),
                          (torch.empty(self.B, self.M, self.topk, dtype=torch.int32).pin_memory(),
                           torch.empty(self.B, self.M, self.topk, dtype=torch.float32).pin_memory()))
 
     def e2e_run(self, din):
-        q, w, k, ks = din
-        if self.kind == "long" and self.world > 1:
-            return self.S.sharded_index_topk(q, w, k, ks, self.lo, self.topk, self.causal, self.start)
-        return self.D.int8_index_topk(q, w, k, ks, topk=self.topk, causal=self.causal, start=self.start - self.lo,
-                                      return_scores=False, key_offset=self.lo)
+        return self._call(*din, return_scores=False)
 
     def roofline(self, kernel_ms, peaks, src, traffic):
         peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
@@ -470,30 +474,77 @@ class IndexWorkload(Workload):
         return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
                 "frac": round(ach / peak, 4), "traffic": traffic.get(self.name),
                 "peak_note": f"dense INT8 = 2 x {src} cuBLAS bf16 burst; achieved counts visible (query, key) "
-                             f"pairs only", "ops_per_launch": ops,
+                             f"pairs only, for the indexer kernel alone", "ops_per_launch": ops,
                 "full_mn_convention_tops": round(self.ops_full / (self.world if self.kind == 'long' else 1)
                                                  / (kernel_ms * 1e-3) / 1e12, 2)}
 
+    def extra(self, dev, ms_step, kern_ms):
+        """The long case: per-stage device times and, key-sharded, a parity check of the merged selection
+        (rank 0) against a one-GPU selection over all keys for the first and last query rows. One GPU:
+        the indexer kernel (its graph replay alone) and the rest of the step (the selection)."""
+        if self.kind != "long":
+            return {}
+        if self.world == 1:
+            return {"stages_ms": {"indexer_kernel": round(kern_ms, 4), "selection": round(ms_step - kern_ms, 4)},
+                    "stages_note": "graph replays: the indexer kernel alone, and the full step minus it"}
+        import torch.distributed as dist
+        q, w, k, ks = self.sets[0]
+        reps = 5
+        names, acc = None, None
+        for _ in range(reps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            marks = []
+            self._call(q, w, k, ks, return_scores=False, events=marks)
+            torch.cuda.synchronize()
+            t, prev = [], e0
+            for _, ev in marks:
+                t.append(prev.elapsed_time(ev))
+                prev = ev
+            names = [n for n, _ in marks]
+            acc = t if acc is None else [a + b for a, b in zip(acc, t)]
+        st = torch.tensor([a / reps for a in acc], dtype=torch.float64, device=dev)
+        if self.world > 1:
+            dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        out = {"stages_ms": {n: round(float(v), 4) for n, v in zip(names, st.tolist())},
+               "stages_note": "eager steps, CUDA events between stages on the launching stream, mean of 5, "
+                              "max over ranks (the timed value above is the graph-captured step)"}
+        if self.world > 1:
+            idx, vals = self._call(q, w, k, ks, return_scores=False)
+            ok = True
+            if self.rank == 0:
+                qh, wh, kh, ksh = self.host
+                kd, ksd = kh.to(dev), ksh.to(dev)
+                for r0 in (0, self.M - 8):
+                    ri, rv = self.D.int8_index_topk(qh[:, r0:r0 + 8].contiguous().to(dev),
+                                                    wh[:, r0:r0 + 8].contiguous().to(dev), kd, ksd, topk=self.topk,
+                                                    causal=True, start=self.start + r0, return_scores=False)
+                    ok = ok and torch.equal(ri, idx[:, r0:r0 + 8]) and torch.equal(rv, vals[:, r0:r0 + 8])
+                del kd, ksd
+            out["parity_ok"] = bool(ok)
+            out["parity_note"] = ("merged selection of query rows 0-7 and 4088-4095 equals (indices and values) a "
+                                  "one-GPU int8_index_topk over all 131072 keys")
+        return out
+
     def cpu_sample(self, seconds):
-        import oracle as O
-        q, w, k, ks = (t.numpy() for t in self.host)
-        rows = np.arange(self.M) if self.M <= 16 else np.linspace(0, self.M - 1, 32).astype(np.int64)
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            sc = O.int8_index_ref(q, w, k, ks, causal=self.causal, start=self.start, rows=rows)
-            O.topk_ref(sc, self.topk) if self.M <= 16 else None
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = (time.perf_counter() - t0) / n
-        if self.causal:
-            sample_pairs = sum(min(self.N, self.start + int(m) + 1) for m in rows)
-        else:
-            sample_pairs = len(rows) * self.N
-        ms_full = dt * 1e3 * (self.pairs / sample_pairs)
-        return ms_full, (f"oracle int8_index_ref (reference.py:27-34) on {len(rows)} of {self.M} query rows, "
-                         f"scaled by visible (query, key) pairs")
+        """The reference's strongest eager indexer on the host (reference.py:72-82 index_torch_int8:
+        torch._int_mm on stacked heads, every key scored) plus torch.topk, on a sample of query rows,
+        scaled to all rows (the eager path has no causal skip)."""
+        from oracle import reference_torch as RT
+        q, w, k, ks = self.host if hasattr(self, "host") else self.host_inputs()
+        nrows = self.M if self.M <= 16 else (16 if self.N <= 8192 else 4)
+        rows = torch.linspace(0, self.M - 1, nrows).long()
+
+        def run():
+            sc = RT.index_torch_int8(q, w, k, ks, rows=rows)
+            if self.causal:
+                keep = torch.arange(self.N)[None, :] <= self.start + rows[:, None]
+                sc = sc.masked_fill(~keep, float("-inf"))
+            torch.topk(sc, min(self.topk, self.N), dim=-1)
+
+        dt, n = timed_loop(run, seconds)
+        return dt * 1e3 * (self.M / nrows), (f"torch on CPU: index_torch_int8 (reference.py:72-82) + torch.topk on "
+                                             f"{nrows} of {self.M} query rows, {n} reps, scaled by rows"), {}
 
 
 class ProducerWorkload(Workload):
@@ -514,6 +565,7 @@ class ProducerWorkload(Workload):
             self.N, self.K = 7168, 2048
             self.metric = "weight_quant GB/s"
             self.bytes = self.N * self.K * 5 + (self.N // 128) * (self.K // 128) * 4
+        self.set_rotation(self.bytes, "inputs")
 
     def config(self):
         if self.kind == "rotate_quant":
@@ -521,7 +573,7 @@ class ProducerWorkload(Workload):
                                 f"fp32 [{self.rows}, 128]"}
         return {"workload": f"weight_quant: 128x128 block int8 of the expert-down weight, fp32 [{self.N}, {self.K}]"}
 
-    def make_host(self):
+    def host_inputs(self):
         g = torch.Generator().manual_seed(3)
         if self.kind == "rotate_quant":
             x = torch.randn(self.rows, 128, generator=g)
@@ -533,20 +585,14 @@ class ProducerWorkload(Workload):
     def prepare(self, dev):
         import deepseek_v32_gtx1650_b200 as D
         self.D = D
-        self.host = self.make_host()
-        self.R = max(2, math.ceil(2 * L2_BYTES / self.bytes))
+        self.host = self.host_inputs()
         self.sets = [self.host.to(dev) for _ in range(self.R)]
-        self.l2_note = f"{self.R} rotating inputs x {self.bytes / 1e6:.1f} MB"
 
     def _run(self, x):
         return self.D.rotate_quant(x) if self.kind == "rotate_quant" else self.D.weight_quant(x)
 
     def step(self, i, ev=None):
-        if ev:
-            ev[0].record()
         self._run(self.sets[i % self.R])
-        if ev:
-            ev[1].record()
 
     def value(self, ms, world):
         return self.bytes * world / (ms * 1e-3) / 1e9
@@ -568,33 +614,28 @@ class ProducerWorkload(Workload):
 
     def cpu_sample(self, seconds):
         import oracle as O
+        host = self.host if hasattr(self, "host") else self.host_inputs()
         if self.kind == "rotate_quant":
             rows = 8192
-            x = self.host[:rows].double().numpy()
+            x = host[:rows].double().numpy()
             fn = lambda: O.rotate_quant_ref(x)  # noqa: E731
             b = rows * 128 * 5 + rows * 4
             what = f"oracle rotate_quant_ref (hadamard_quant.py:106-110) on {rows} of {self.rows} vectors"
         else:
             nr = 1024
-            x = self.host[:nr].numpy()
+            x = host[:nr].numpy()
             fn = lambda: O.weight_quant_ref(x)  # noqa: E731
             b = nr * self.K * 5 + (nr // 128) * (self.K // 128) * 4
             what = f"oracle weight_quant_ref (test_kernels.py:80-82) on {nr} of {self.N} rows"
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            fn()
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = time.perf_counter() - t0
-        return b * n / dt / 1e9, f"{what}, {n} reps"
+        dt, n = timed_loop(fn, seconds)
+        return b / dt / 1e9, f"{what}, {n} reps", {}
 
 
 class IndexStepWorkload(Workload):
     """The reference's end-to-end indexer step (bench_indexer_e2e.py:46-58) at the 4096^2 causal
     prefill: rotate + quantise the 4096 new keys into the int8 cache and the fp32 queries
-    [1, 4096, 64, 128], fold the query scales into the head weights, score, select the top-2048."""
+    [1, 4096, 64, 128] (the query scales folded into the head weights inside the producer), score,
+    select the top-2048."""
     higher_is_better = False
     dtype = "fp32->int8"
     launches_per_step = 4  # rotate_quant (keys), rotate_quant (queries), int8_index, top-k
@@ -606,12 +647,13 @@ class IndexStepWorkload(Workload):
         self.unit = "ms"
         self.pairs = sum(m + 1 for m in range(self.M))
         self.ops = 2.0 * self.pairs * self.H * 128
+        self.l2_note = "one input set of 136 MB (> L2): q 134 MB fp32 is read once per step"
 
     def config(self):
         return {"workload": f"indexer step: B=1 M={self.M} new keys={self.N} H=64 D=128 causal, fp32 q/k, "
                             f"top-{self.topk}", "visible_pairs": self.pairs}
 
-    def make_host(self):
+    def host_inputs(self):
         g = torch.Generator().manual_seed(0)
         q = torch.randn(self.B, self.M, self.H, 128, generator=g)
         k = torch.randn(self.B, self.N, 128, generator=g)
@@ -622,26 +664,20 @@ class IndexStepWorkload(Workload):
     def prepare(self, dev):
         import deepseek_v32_gtx1650_b200 as D
         self.D = D
-        self.host = self.make_host()
+        self.host = self.host_inputs()
         q, k, w = (t.to(dev) for t in self.host)
         self.dev_in = (q, k, w)
         self.cache = D.KeyCache(self.B, self.N, dev)
         self.cache.append(k)  # the dominant-kernel replay reads the quantised cache and queries
-        self._qq, qs = D.rotate_quant(q)
-        self._w2 = (w * qs).contiguous()
-        self.l2_note = "one input set of 136 MB (> L2): q 134 MB fp32 is read once per step"
+        self._qq, self._w2 = D.rotate_quant(q, scale_mul=w)
 
     def step(self, i, ev=None, main_only=False):
         q, k, w = self.dev_in
         if main_only:  # the dominant kernel alone: scores of the already quantised cache and queries
             self.D.int8_index(self._qq, self._w2, self.cache.k, self.cache.k_s, causal=True, start=0)
             return
-        if ev:
-            ev[0].record()
         self.cache.length = 0
         self.D.indexer_step(q, w, self.cache, k, topk=self.topk)
-        if ev:
-            ev[1].record()
 
     def value(self, ms, world):
         return ms
@@ -665,106 +701,111 @@ class IndexStepWorkload(Workload):
                              f"visible (query, key) pairs", "ops_per_launch": self.ops}
 
     def cpu_sample(self, seconds):
-        import oracle as O
-        q, k, w = self.host
-        rows = np.linspace(0, self.M - 1, 16).astype(np.int64)
-        t0 = time.perf_counter()
-        n = 0
-        qfull = np.zeros((self.B, self.M, self.H, 128), dtype=np.int8)
-        wfull = np.zeros((self.B, self.M, self.H), dtype=np.float32)
-        while True:
-            kq, ks = O.rotate_quant_ref(k.double().numpy())
-            qq, qs = O.rotate_quant_ref(q[:, rows].double().numpy())
-            qfull[:, rows] = qq
-            wfull[:, rows] = w[:, rows].numpy() * qs
-            O.int8_index_ref(qfull, wfull, kq, ks, causal=True, start=0, rows=rows)
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = (time.perf_counter() - t0) / n
-        sample_pairs = sum(int(m) + 1 for m in rows)
-        ms_full = dt * 1e3 * (self.pairs / sample_pairs)
-        return ms_full, (f"oracle rotate_quant_ref + int8_index_ref on {len(rows)} of {self.M} query rows (all "
-                         f"keys quantised), scaled by visible (query, key) pairs")
+        """Host version of the step with the reference's eager pieces: the rotation as an fp32 matmul
+        with the Hadamard matrix plus per-vector quantisation (hadamard_quant.py:106-110 in fp32), then
+        index_torch_int8 (reference.py:72-82) and torch.topk on a sample of query rows, scaled by rows."""
+        from oracle import reference_torch as RT
+        from deepseek_v32_gtx1650_b200 import workloads as W
+        q, k, w = self.host if hasattr(self, "host") else self.host_inputs()
+        Hm = W.hadamard(128).float()
+        rows = torch.linspace(0, self.M - 1, 16).long()
+
+        def rq(x):
+            xr = x @ Hm
+            s = xr.abs().amax(-1).clamp_min(1e-4) / 127.0
+            return torch.clamp(torch.round(xr / s[..., None]), -127, 127).to(torch.int8), s
+
+        def run():
+            kq, ks = rq(k)
+            qq, qs = rq(q[:, rows])
+            sc = RT.index_torch_int8(qq, w[:, rows] * qs, kq, ks)
+            keep = torch.arange(self.N)[None, :] <= rows[:, None]
+            torch.topk(sc.masked_fill(~keep, float("-inf")), self.topk, dim=-1)
+
+        dt, n = timed_loop(run, seconds)
+        return dt * 1e3 * (self.M / len(rows)), (f"torch on CPU: fp32 Hadamard matmul + quantise of all keys and "
+                                                 f"{len(rows)} of {self.M} query rows, index_torch_int8 "
+                                                 f"(reference.py:72-82) + torch.topk, {n} reps, scaled by rows"), {}
 
 
-def make_workload(args, rank, world):
-    if args.workload == "gemm_up":
+def make_workload(name, args, rank, world):
+    if name == "gemm_up":
         return GemmWorkload(4096, 2048, 7168, "bf16", rank, world, "expert_up")
-    if args.workload == "gemm_down":
+    if name == "gemm_down":
         return GemmWorkload(args.m, 7168, 2048, args.out, rank, world, f"expert_down_m{args.m}", seed=1)
-    if args.workload == "act_quant":
+    if name == "act_quant":
         return ActQuantWorkload(2048, 7168, args.aq_dtype, rank, world)
-    if args.workload in ("index_prefill", "index_decode", "index_long"):
-        return IndexWorkload(args.workload.split("_")[1], rank, world)
-    if args.workload in ("rotate_quant", "weight_quant"):
-        return ProducerWorkload(args.workload, rank, world)
-    if args.workload == "index_step":
+    if name in ("act_quant_fp32", "act_quant_bf16"):
+        return ActQuantWorkload(2048, 7168, name.split("_")[-1], rank, world)
+    if name in ("index_prefill", "index_decode", "index_long"):
+        return IndexWorkload(name.split("_")[1], rank, world)
+    if name in ("rotate_quant", "weight_quant"):
+        return ProducerWorkload(name, rank, world)
+    if name == "index_step":
         return IndexStepWorkload(rank, world)
-    raise SystemExit(f"unknown workload {args.workload}")
+    raise SystemExit(f"unknown workload {name}")
+
+
+def secondary_names(args, world):
+    """The rest of BASELINE's metric beside the headline GEMM: at one GPU the indexer prefill step,
+    act_quant fp32 / bf16 and the long-context indexer; at N GPUs the key-sharded long indexer."""
+    if args.workload != "gemm_up" or args.no_secondary:
+        return []
+    if world == 1:
+        return ["index_prefill", "act_quant_fp32", "act_quant_bf16", "index_long"]
+    return ["index_long"]
 
 
 # ------------------------------------------------------------------------------------------ arms
+def ref_entry(wl, args, world, cores):
+    for _ in range(args.warmup):
+        wl.cpu_sample(0.0)
+    vals = []
+    t0 = time.perf_counter()
+    sample, variants = "", {}
+    for _ in range(args.steps):
+        v, sample, variants = wl.cpu_sample(args.ref_step_seconds)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    v = statistics.median(vals)
+    cb = {"value": round(v, 4), "unit": wl.unit, "cores": cores, "kind": "port", "sample": sample,
+          "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+    if variants:
+        cb["variants"] = variants
+    return {"metric": wl.metric, "value": round(v, 4), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 2),
+            "higher_is_better": wl.higher_is_better, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
+            "data": "synthetic (seeded)", "config": wl.config_full(), "cpu_baseline": cb,
+            "e2e": {"value": round(v, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    try:
-        from threadpoolctl import threadpool_limits
-        threadpool_limits(os.cpu_count())
-    except Exception:
-        pass
-    wl = make_workload(args, 0, 1)
-    # inputs on the CPU only
-    import deepseek_v32_gtx1650_b200.workloads as W  # noqa: F401
-    if isinstance(wl, GemmWorkload):
-        x, B, b_s = W.gemm_inputs(wl.M, wl.N, wl.K, seed=wl.seed)
-        wl.host = (x, B, b_s)
-    elif isinstance(wl, ActQuantWorkload):
-        wl.host = W.act_quant_input(wl.M, wl.N).to(wl.tdt)
-    elif hasattr(wl, "make_host"):
-        wl.host = wl.make_host()
-    else:
-        wl.host = W.index_inputs(wl.B, wl.M, wl.N, seed=0)
-    per = args.ref_step_seconds
-    for _ in range(args.warmup):
-        wl.cpu_sample(0.0)
-    vals = []
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        v, sample = wl.cpu_sample(per)
-        vals.append(v)
-    wall = time.perf_counter() - t0
-    v = statistics.median(vals)
-    cores = cpu_threads()
-    line = {"impl": "reference", "metric": wl.metric, "value": round(v, 4), "unit": wl.unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 2),
-            "higher_is_better": wl.higher_is_better, "scaling": wl.scaling, "vs_baseline": None,
-            "dtype": wl.dtype, "data": "synthetic (seeded)",
-            "config": wl.config(),
-            "cpu_baseline": {"value": round(v, 4), "unit": wl.unit, "cores": cores, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": round(v, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    cores = cpu_setup()
+    line = ref_entry(make_workload(args.workload, args, 0, world), args, world, cores)
+    line["impl"] = "reference"
+    sec = []
+    for name in secondary_names(args, world):
+        a2 = argparse.Namespace(**vars(args))
+        a2.steps = 1
+        a2.warmup = 0
+        e = ref_entry(make_workload(name, args, 0, world), a2, world, cores)
+        sec.append({k: e[k] for k in ("metric", "value", "unit", "higher_is_better", "config", "cpu_baseline")})
+    if sec:
+        line["secondary"] = sec
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
+def measure(wl, args, dev, world, rank, local, peaks, src, traffic, cpu_seconds):
+    """Warm-up, K timed steps (one CUDA graph, max over ranks), clocks, dominant-kernel roofline, e2e
+    through the public API and (one GPU, rank 0) the CPU baseline of one workload. Every rank runs the
+    same collectives. Returns the entry on rank 0 (None elsewhere)."""
     import torch.distributed as dist
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        from datetime import timedelta
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     import deepseek_v32_gtx1650_b200 as D
-    wl = make_workload(args, rank, world)
     wl.prepare(dev)
-    peaks, src = load_peaks()
-    traffic = load_traffic()
 
     def barrier():
         if world > 1:
@@ -775,8 +816,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     code = D.device_status(local)
     if code:
-        raise SystemExit(f"kernel reported an internal wait timeout during warm-up: {code:#x}")
-
+        raise SystemExit(f"{wl.name}: kernel reported an internal wait timeout during warm-up: {code:#x}")
     sampler = ClockSampler(local)
 
     def capture(fn):
@@ -793,55 +833,35 @@ def run_ours(args):
         torch.cuda.synchronize()
         return g
 
-    graph = kgraph = None
-    if wl.graphable:
-        graph = capture(lambda: [wl.step(i) for i in range(args.steps)])
-        if wl.launches_per_step > 1:
-            kgraph = capture(lambda: [wl.step(i, main_only=True) for i in range(args.steps)])
-        # One untimed replay of each graph: the first launch of an instantiated graph also uploads it.
-        for g in (graph, kgraph):
-            if g is not None:
-                g.replay()
-        torch.cuda.synchronize()
-    evs = None if graph is not None else [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                                          for _ in range(args.steps)]
+    graph = capture(lambda: [wl.step(i) for i in range(args.steps)])
+    kgraph = capture(lambda: [wl.step(i, main_only=True) for i in range(args.steps)]) \
+        if wl.launches_per_step > 1 else None
+    for g in (graph, kgraph):  # the first launch of an instantiated graph also uploads it
+        if g is not None:
+            g.replay()
+    torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     sampler.start()
     t_start.record()
-    if graph is not None:
-        graph.replay()
-    else:
-        for i in range(args.steps):
-            wl.step(i, evs[i])
+    graph.replay()
     t_end.record()
     torch.cuda.synchronize()
     barrier()
     sampler.stop()
     ms = t_start.elapsed_time(t_end)
-    if graph is not None:
-        if kgraph is not None:  # the dominant kernel alone, back to back
-            k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            k0.record()
-            kgraph.replay()
-            k1.record()
-            torch.cuda.synchronize()
-            kern_ms = k0.elapsed_time(k1) / args.steps
-        else:
-            kern_ms = ms / args.steps
-    elif wl.launches_per_step > 1:  # eager steps (collectives): the dominant kernel alone, back to back
+    if kgraph is not None:  # the dominant kernel alone, back to back
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         k0.record()
-        for i in range(args.steps):
-            wl.step(i, main_only=True)
+        kgraph.replay()
         k1.record()
         torch.cuda.synchronize()
         kern_ms = k0.elapsed_time(k1) / args.steps
     else:
-        kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        kern_ms = ms / args.steps
     window = "timed region"
-    # timed region too short for NVML: sample a soak of the same step. Decided and sized identically on
+    # timed region too short for NVML: sample a soak of the same graph. Decided and sized identically on
     # every rank (a step may hold collectives, which every rank must run the same number of times).
     t = torch.tensor([ms, kern_ms, 1.0 if (len(sampler.samples) < 5 and not args.profile) else 0.0], device=dev,
                      dtype=torch.float64)
@@ -849,18 +869,17 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kern_ms, need_soak = float(t[0]), float(t[1]), bool(t[2] > 0)
     if need_soak:
-        window = "soak of the same step right after the timed region (timed region too short for NVML)"
-        reps = max(1, min(100000, int(600.0 / max(ms if graph is not None else ms / args.steps, 1e-3))))
+        window = "soak of the same graph right after the timed region (timed region too short for NVML)"
+        reps = max(1, min(100000, int(600.0 / max(ms, 1e-3))))
         sampler.start()
         for i in range(reps):
-            if graph is not None:
-                graph.replay()
-            else:
-                wl.step(i)
+            graph.replay()
             if i % 64 == 63:
                 torch.cuda.synchronize()
         torch.cuda.synchronize()
         sampler.stop()
+    del graph, kgraph  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     ms_step = ms / args.steps
     value = wl.value(ms_step, world)
 
@@ -881,40 +900,67 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     e2e_val = wl.value(float(e_ms), world)
+    extra = {} if args.profile else wl.extra(dev, ms_step, kern_ms)
     code = D.device_status(local)
 
-    line = None
+    entry = None
     if rank == 0:
-        line = {"metric": wl.metric, "value": round(value, 4), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": wl.higher_is_better,
-                "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
-                "data": "synthetic (seeded generators with the BASELINE shapes and distributions)",
-                "config": dict(wl.config(), l2=wl.l2_note),
-                "e2e": {"value": round(e2e_val, 4), "unit": wl.unit, "h2d_bytes_per_step": int(wl.h2d),
-                        "d2h_bytes_per_step": int(wl.d2h), "steps": e2e_steps,
-                        "mode": "two-deep pipeline: step j+1's host-to-device copy and step j-1's "
-                                "device-to-host copy overlap step j's call"},
-                "roofline": wl.roofline(kern_ms, peaks, src, traffic),
-                "gpu_launches": args.steps * wl.launches_per_step,
-                "timing": "CUDA graph of the K steps, replayed once between events" if graph is not None
-                          else "eager launches, CUDA events per launch",
-                "clocks": sampler.summary(window),
-                "device_error_word": code}
-        if world == 1 and not args.no_cpu_baseline:
-            try:
-                from threadpoolctl import threadpool_limits
-                threadpool_limits(os.cpu_count())
-            except Exception:
-                pass
-            v, sample = wl.cpu_sample(args.cpu_seconds)
-            line["cpu_baseline"] = {"value": round(v, 4), "unit": wl.unit, "cores": cpu_threads(), "kind": "port",
-                                    "sample": sample}
-    del graph, kgraph  # graphs holding NCCL calls go before the process group
-    torch.cuda.synchronize()
+        entry = {"metric": wl.metric, "value": round(value, 4), "unit": wl.unit, "n_gpus": world,
+                 "ms_per_step": round(ms_step, 5), "higher_is_better": wl.higher_is_better, "scaling": wl.scaling,
+                 "dtype": wl.dtype, "config": wl.config_full(),
+                 "e2e": {"value": round(e2e_val, 4), "unit": wl.unit, "h2d_bytes_per_step": int(wl.h2d),
+                         "d2h_bytes_per_step": int(wl.d2h), "steps": e2e_steps,
+                         "mode": "two-deep pipeline: step j+1's host-to-device copy and step j-1's "
+                                 "device-to-host copy overlap step j's call"},
+                 "roofline": wl.roofline(kern_ms, peaks, src, traffic),
+                 "gpu_launches": args.steps * wl.launches_per_step,
+                 "timing": "CUDA graph of the K steps, replayed once between events",
+                 "clocks": sampler.summary(window),
+                 "device_error_word": code}
+        entry.update(extra)
+        if world == 1 and cpu_seconds > 0:
+            cores = cpu_setup()
+            v, sample, variants = wl.cpu_sample(cpu_seconds)
+            entry["cpu_baseline"] = {"value": round(v, 4), "unit": wl.unit, "cores": cores, "kind": "port",
+                                     "sample": sample, "os_cpu_count": os.cpu_count()}
+            if variants:
+                entry["cpu_baseline"]["variants"] = variants
+    wl.release()
+    torch.cuda.empty_cache()
+    return entry
+
+
+def run_ours(args):
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, src = load_peaks()
+    traffic = load_traffic()
+    cpu_s = 0.0 if args.no_cpu_baseline else args.cpu_seconds
+    line = measure(make_workload(args.workload, args, rank, world), args, dev, world, rank, local, peaks, src,
+                   traffic, cpu_s)
+    sec = []
+    for name in secondary_names(args, world):
+        e = measure(make_workload(name, args, rank, world), args, dev, world, rank, local, peaks, src, traffic,
+                    min(cpu_s, 5.0))
+        if e is not None:
+            sec.append(e)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    if line is not None:
+    if rank == 0:
+        line.update({"steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
+                     "data": "synthetic (seeded generators with the BASELINE shapes and distributions)"})
+        if sec:
+            line["secondary"] = sec
+            line["gpu_launches_all_entries"] = line["gpu_launches"] + sum(e["gpu_launches"] for e in sec)
         print(json.dumps(line), flush=True)
 
 
@@ -933,11 +979,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="the headline workload only")
     ap.add_argument("--profile", action="store_true",
-                    help="for ncu captures: timed steps only (no clock soak, e2e or CPU baseline)")
+                    help="for ncu captures: timed steps only (no clock soak, e2e, secondaries or CPU baseline)")
     args = ap.parse_args()
     if args.profile:
         args.no_cpu_baseline = True
+        args.no_secondary = True
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         run_reference_arm(args)

@@ -33,16 +33,18 @@ SIGNATURES = {
     "dsv32_int8_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "dsv32_int8_gemm_noalloc": (_i32, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _p]),
     "dsv32_int8_gemm_partials": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p]),
-    "dsv32_int8_index": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _p]),
-    "dsv32_topk": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p]),
-    "dsv32_int8_index_topk": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _i64,
-                                     _p, _p, _p]),
-    "dsv32_rotate_quant": (_i32, [_p, _i32, _i64, _i32, _p, _p, _p]),
+    "dsv32_int8_index": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _p]),
+    "dsv32_topk_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32]),
+    "dsv32_topk": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p]),
+    "dsv32_int8_index_topk": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _i32,
+                                     _i64, _i64, _p, _p, _p, _i64, _p]),
+    "dsv32_rotate_quant": (_i32, [_p, _i32, _i64, _i32, _p, _p, _p, _p]),
     "dsv32_weight_quant": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p]),
     "dsv32_device_status": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint32)]),
     "dsv32_status_string": (ctypes.c_char_p, [_i32]),
     "dsv32_last_error_message": (ctypes.c_char_p, []),
-    "dsv32_topk_parts": (_i32, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "dsv32_topk_parts": (_i32, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _i64, _i64, _i64, _i64, _p, _p, _p,
+                                _i64, _p]),
     "dsv32_device_alloc": (_i32, [_i64, ctypes.POINTER(_p)]),
     "dsv32_device_free": (_i32, [_p]),
     "dsv32_ipc_export": (_i32, [_p, _p]),
@@ -51,7 +53,7 @@ SIGNATURES = {
     "dsv32_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 IPC_HANDLE_BYTES = 64
 
 _LIB = None

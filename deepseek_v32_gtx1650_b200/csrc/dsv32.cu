@@ -4,6 +4,7 @@
 // device error word g_dsv32_device_error. Host side: argument validation (the reference's
 // asserts), TMA tensor-map encoding through the driver entry point (no -lcuda needed),
 // per-device launch set-up, and the launches themselves.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -14,6 +15,7 @@
 #include "../../include/dsv32_int8.h"
 #include "act_quant.cuh"
 #include "int8_gemm.cuh"
+#include "int8_gemm_swap.cuh"
 #include "int8_index.cuh"
 #include "topk.cuh"
 #include "producers.cuh"
@@ -85,6 +87,12 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<256, true>, gemm::Smem<256>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<128, false>, gemm::Smem<128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_kernel<128, true>, gemm::Smem<128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<16, false>, gemm::SwapSmem<16>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<16, true>, gemm::SwapSmem<16>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<32, false>, gemm::SwapSmem<32>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<32, true>, gemm::SwapSmem<32>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, false>, gemm::SwapSmem<64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, true>, gemm::SwapSmem<64>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128>, index::Cfg<64, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128>, index::Cfg<32, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128>, index::Cfg<16, 128>::kAlloc));
@@ -168,6 +176,7 @@ int launch(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
 
 struct GemmPlan {
   int BN;
+  int swap_mn;  // > 0: decode-sized m on the swapped kernel, tokens padded to this many
   int64_t tiles, units;
   int grid;
   bool split;
@@ -176,27 +185,31 @@ struct GemmPlan {
   int64_t ws_bytes;  // workspace the stream-K schedule needs (0 when data-parallel)
 };
 
-// Tile width and schedule for an (m, n, k) problem on this device. Stream-K only when there are
-// fewer tiles than SMs (decode-sized m): there it is the only way to use every SM. With at least a
-// wave of tiles, whole tiles per SM measured faster on B200 than splitting tiles (the partial-tile
-// round trip through the workspace costs more than the tail wave it removes).
+// Tile width and schedule for an (m, n, k) problem on this device. m <= 64 runs the swapped kernel
+// (weight rows on the UMMA M side, the tokens padded to 16, 32 or 64 on the N side) instead of
+// padding the tokens to 128-row tiles. Stream-K only when there are fewer tiles than SMs
+// (decode-sized m): there it is the only way to use every SM. With at least a wave of tiles, whole
+// tiles per SM measured faster on B200 than splitting tiles (the partial-tile round trip through
+// the workspace costs more than the tail wave it removes).
 GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k, int num_sms,
                    int64_t ws_tiles_cap = dsv32::gemm::kMaxSplitTiles, int slot_rows = dsv32::gemm::kBM) {
   GemmPlan p;
+  p.swap_mn = m <= 16 ? 16 : m <= 32 ? 32 : m <= dsv32::gemm::kSwMaxM ? 64 : 0;
   // 128x256 tiles when they fill the GPU; otherwise 128x128 tiles (twice as many, so small-M problems
   // split K less: measured 25.1 -> 16.8 us at M=32 and 29.4 -> 20.6 us at M=512, N=7168, K=2048).
   // For full waves the wider tile wins (71 vs 106 us at 4096x2048x7168: a 128-wide MMA re-reads A
   // from shared memory twice as often).
   const int64_t tiles256 = ((m + 127) / 128) * (n / 256);
-  p.BN = (n % 256 == 0 && tiles256 >= num_sms) ? 256 : 128;
-  p.tiles = ((m + 127) / 128) * ((n + p.BN - 1) / p.BN);
+  p.BN = (n % 256 == 0 && tiles256 >= num_sms && !p.swap_mn) ? 256 : 128;
+  p.tiles = ((m + 127) / 128) * ((n + p.BN - 1) / p.BN);  // swapped: n / 128 weight tiles, one token tile
   p.units = p.tiles * (k / 128);
   p.split = p.tiles < num_sms && p.tiles <= ws_tiles_cap;
   p.slot_rows = slot_rows;
   p.ws_tiles_cap = ws_tiles_cap;
   if (p.split) {
     p.grid = static_cast<int>(p.units < num_sms ? p.units : num_sms);
-    p.ws_bytes = dsv32::gemm::workspace_bytes(p.BN, p.grid, ws_tiles_cap, p.slot_rows);
+    p.ws_bytes = p.swap_mn ? dsv32::gemm::swap_workspace_bytes(p.swap_mn, p.grid, ws_tiles_cap)
+                           : dsv32::gemm::workspace_bytes(p.BN, p.grid, ws_tiles_cap, p.slot_rows);
   } else {
     p.grid = static_cast<int>(p.tiles < num_sms ? p.tiles : num_sms);
     p.ws_bytes = 0;
@@ -222,7 +235,7 @@ int gemm_launch(const GemmPlan& plan, const int8_t* a, const float* a_s, const i
   const uint64_t dimsA[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
   const uint64_t dimsB[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
   const uint64_t strides[1] = {static_cast<uint64_t>(k)};
-  const uint32_t boxA[2] = {128, 128};
+  const uint32_t boxA[2] = {128, static_cast<uint32_t>(plan.swap_mn ? plan.swap_mn : 128)};
   const uint32_t boxB[2] = {128, static_cast<uint32_t>(plan.BN)};
   if (int st = encode_i8_map(&tmA, a, 2, dimsA, strides, boxA)) return st;
   if (int st = encode_i8_map(&tmB, b, 2, dimsB, strides, boxB)) return st;
@@ -233,6 +246,20 @@ int gemm_launch(const GemmPlan& plan, const int8_t* a, const float* a_s, const i
   const uint32_t ok = partials ? kOutF32 : static_cast<uint32_t>(c_dtype);
   const int cap = static_cast<int>(plan.ws_tiles_cap), sr = plan.slot_rows;
   const unsigned g = static_cast<unsigned>(plan.grid);
+  if (plan.swap_mn) {
+    const char* sw = "int8_gemm_swap_kernel launch";
+#define DSV32_SWAP_CASE(MN)                                                                                      \
+  if (plan.swap_mn == MN)                                                                                        \
+    return partials ? launch(int8_gemm_swap_kernel<MN, true>, g, kSwThreads, SwapSmem<MN>::kAlloc, st, sw, tmA, tmB, \
+                             a_s, b_s, c, ok, mi, ni, ki, partials, ws, cap)                                     \
+                    : launch(int8_gemm_swap_kernel<MN, false>, g, kSwThreads, SwapSmem<MN>::kAlloc, st, sw, tmA,  \
+                             tmB, a_s, b_s, c, ok, mi, ni, ki, static_cast<int32_t*>(nullptr), ws, cap);
+    DSV32_SWAP_CASE(16)
+    DSV32_SWAP_CASE(32)
+    DSV32_SWAP_CASE(64)
+#undef DSV32_SWAP_CASE
+    return DSV32_ERR_UNSUPPORTED;
+  }
   const char* what = "int8_gemm_kernel launch";
   if (plan.BN == 256) {
     if (partials)
@@ -269,7 +296,8 @@ int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b
 
 template <int H, int D>
 int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w, const float* k_s, float* out,
-                 int64_t batch, int64_t m, int64_t n, int causal, int64_t start, int num_sms, cudaStream_t st) {
+                 int64_t batch, int64_t m, int64_t n, int causal, int64_t start, int64_t k_ld, int fill_masked,
+                 int num_sms, cudaStream_t st) {
   using namespace dsv32::index;
   using C = Cfg<H, D>;
   const int64_t nqb = (m + C::QB - 1) / C::QB;
@@ -287,13 +315,18 @@ int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w,
   return launch(int8_index_kernel<H, D>, static_cast<unsigned>(grid), kThreads, C::kAlloc, st,
                 "int8_index_kernel launch", tmQ, tmK, w, k_s, out, static_cast<int>(m), static_cast<int>(n), causal,
                 static_cast<long long>(start), static_cast<int>(tpc), static_cast<int>(chunks),
-                static_cast<int>(units));
+                static_cast<int>(units), static_cast<long long>(k_ld), fill_masked);
 }
 
+// k_ld: keys between the starts of consecutive batches of k and k_s (0: n, the contiguous layout).
+// fill_masked == 0: key tiles no query of a block can see are left unwritten in `out`.
 int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
-               int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, void* stream) {
+               int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, int64_t k_ld,
+               int fill_masked, void* stream) {
   if (!q || !w || !k || !k_s || !out) return DSV32_ERR_INVALID_ARG;
   if (batch < 1 || m < 1 || n < 1) return DSV32_ERR_INVALID_ARG;
+  if (k_ld == 0) k_ld = n;
+  if (k_ld < n) return DSV32_ERR_INVALID_ARG;
   if (!((heads == 16 || heads == 32 || heads == 64) && (dim == 64 || dim == 128))) return DSV32_ERR_UNSUPPORTED;
   if (m * heads > (1LL << 31) - 1 || n > (1LL << 31) - 1 || batch > 65535) return DSV32_ERR_UNSUPPORTED;
   if (!aligned16(q) || !aligned16(k)) return DSV32_ERR_INVALID_ARG;
@@ -307,14 +340,15 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
   const uint64_t strQ[2] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(m * heads * dim)};
   const uint32_t boxQ[3] = {static_cast<uint32_t>(dim), static_cast<uint32_t>(qb * heads), 1};
   const uint64_t dimsK[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(n), static_cast<uint64_t>(batch)};
-  const uint64_t strK[2] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(n * dim)};
+  const uint64_t strK[2] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(k_ld * dim)};
   const uint32_t boxK[3] = {static_cast<uint32_t>(dim), 128, 1};
   if (int st = encode_i8_map(&tmQ, q, 3, dimsQ, strQ, boxQ)) return st;
   if (int st = encode_i8_map(&tmK, k, 3, dimsK, strK, boxK)) return st;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int S = info->num_sms;
-#define DSV32_INDEX_CASE(HH, DD) \
-  if (heads == HH && dim == DD) return index_launch<HH, DD>(tmQ, tmK, w, k_s, out, batch, m, n, causal, start, S, st);
+#define DSV32_INDEX_CASE(HH, DD)                                                                              \
+  if (heads == HH && dim == DD)                                                                               \
+    return index_launch<HH, DD>(tmQ, tmK, w, k_s, out, batch, m, n, causal, start, k_ld, fill_masked, S, st);
   DSV32_INDEX_CASE(64, 128)
   DSV32_INDEX_CASE(32, 128)
   DSV32_INDEX_CASE(16, 128)
@@ -347,27 +381,75 @@ int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const in
                 out_val, causal_m, cs, cr0, seg_len, nseg, parts);
 }
 
-constexpr int kTopkRegMax = 512 * 16;                  // longest row a register pass holds
-constexpr int64_t kTopkTempBytes = int64_t(256) << 20;  // stream-ordered scratch per row batch
+constexpr int kTopkRegMax = 512 * 16;                       // longest row a register pass holds
+constexpr int64_t kTopkPreferredBytes = int64_t(256) << 20;  // workspace the library asks for, at most
+
+// Stage plan for rows longer than one register pass: each row is cut into equal segments of at most
+// 8192 positions, every segment keeps its own top-k (a superset of the row's top-k within it), and the
+// segment lists, contiguous and in position order, are merged by the next stage until one pass
+// remains. Candidates keep global positions and their order, so ties resolve exactly as in a single
+// pass. Stage outputs live in the caller's workspace: two ping-pong buffers of (id, value) candidates,
+// `per_row` bytes per row of a row batch.
+struct TopkPlan {
+  int stages = 0;
+  int nseg[8] = {}, seg[8] = {}, n[9] = {};
+  bool ok = true;        // a staged plan exists (or none is needed)
+  int64_t per_row = 0;   // workspace bytes per row (0: one register pass)
+};
+
+TopkPlan topk_plan(int n, int k, bool parts) {
+  TopkPlan p;
+  p.n[0] = n;
+  while (p.n[p.stages] > kTopkRegMax) {
+    const int cur = p.n[p.stages];
+    const int nseg = (cur + kTopkRegMax - 1) / kTopkRegMax;
+    // segment starts on 16-position boundaries when the first pass reads lists (a thread's 16
+    // positions must not straddle two lists), else on 4-position (16-byte) boundaries
+    const int align = (parts && p.stages == 0) ? 15 : 3;
+    const int seg = ((cur + nseg - 1) / nseg + align) & ~align;
+    if (p.stages == 8 || cur - (nseg - 1) * seg < k || static_cast<int64_t>(nseg) * k >= cur) {
+      p.ok = false;
+      return p;
+    }
+    p.nseg[p.stages] = nseg;
+    p.seg[p.stages] = seg;
+    p.n[p.stages + 1] = nseg * k;
+    ++p.stages;
+  }
+  p.per_row = p.stages ? 2 * static_cast<int64_t>(p.n[1]) * 8 : 0;
+  return p;
+}
+
+// Workspace bytes the top-k of `rows` rows of n positions wants (0: none), or -status.
+int64_t topk_ws_bytes(int64_t rows, int64_t n, int64_t k, int nparts) {
+  if (rows < 1 || n < 1 || k < 1 || k > n) return -DSV32_ERR_INVALID_ARG;
+  if (n > (1LL << 31) - 1) return -DSV32_ERR_UNSUPPORTED;
+  const TopkPlan p = topk_plan(static_cast<int>(n), static_cast<int>(k), nparts > 0);
+  if (!p.ok) return nparts > 0 ? -DSV32_ERR_UNSUPPORTED : 0;  // plain rows: the long-row kernel
+  if (p.per_row == 0) return 0;
+  int64_t batch = kTopkPreferredBytes / p.per_row;
+  if (batch < 1) batch = 1;
+  if (batch > rows) batch = rows;
+  return batch * p.per_row;
+}
 
 // causal_m > 0: row r (= b * causal_m + m) has its scores past key causal_start + m masked to -inf
 // (the indexer's causal rows); those positions are treated as -inf without being read.
 //
-// Rows longer than one register pass are selected in stages: each row is cut into equal segments
-// of at most 8192 positions, every segment keeps its own top-k (a superset of the row's top-k
-// within it), and the segment lists, contiguous and in position order, are merged by the next
-// stage until one pass remains. Candidates keep global positions and their order, so ties resolve
-// exactly as in a single pass. Stage outputs live in stream-ordered scratch (cudaMallocAsync),
-// processed in row batches of at most 256 MB; if the scratch cannot be had, or a segment would be
-// shorter than k, the long-row kernel re-reads the row from L2 instead.
+// Rows longer than one register pass run the staged plan in row batches sized to the workspace. With
+// no workspace, or one smaller than a single row needs, or no staged plan (a segment shorter than k),
+// plain rows go to the long-row kernel, which re-reads the row from L2 and needs no scratch; rows
+// given as lists (parts) then return DSV32_ERR_UNSUPPORTED. Nothing is allocated here.
 int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
-              int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream, int64_t causal_m = 0,
-              int64_t causal_start = 0, const dsv32::topk::RowParts* parts = nullptr) {
+              int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* workspace, int64_t ws_bytes,
+              void* stream, int64_t causal_m = 0, int64_t causal_start = 0,
+              const dsv32::topk::RowParts* parts = nullptr) {
   const dsv32::topk::RowParts no_parts{};
   const dsv32::topk::RowParts& p0 = parts ? *parts : no_parts;  // addressing of the first pass
   if ((!scores && !parts) || !out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
   if (rows < 1 || n < 1 || k < 1 || k > n || (!parts && ld < n)) return DSV32_ERR_INVALID_ARG;
   if (cand_idx && cand_ld < n) return DSV32_ERR_INVALID_ARG;
+  if (workspace && (!aligned16(workspace) || ws_bytes < 0)) return DSV32_ERR_INVALID_ARG;
   if (n > (1LL << 31) - 1 || rows > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
   int dev = 0;
   DeviceInfo* info = nullptr;
@@ -380,78 +462,50 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
     return topk_reg_launch(scores, rows, nn, ld, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, causal_start,
                            0, nn, 1, st, p0);
   }
-  // Stage plan: segment counts until the candidate list fits one register pass.
-  int plan_nseg[8], plan_seg[8], plan_n[9];
-  int stages = 0;
-  bool staged_ok = true;
-  plan_n[0] = nn;
-  while (plan_n[stages] > kTopkRegMax) {
-    const int cur = plan_n[stages];
-    const int nseg = (cur + kTopkRegMax - 1) / kTopkRegMax;
-    // segment starts on 16-position boundaries when the first pass reads lists (a thread's 16
-    // positions must not straddle two lists), else on 4-position (16-byte) boundaries
-    const int align = (parts && stages == 0) ? 15 : 3;
-    const int seg = ((cur + nseg - 1) / nseg + align) & ~align;
-    if (stages == 8 || cur - (nseg - 1) * seg < kk || static_cast<int64_t>(nseg) * kk >= cur) {
-      staged_ok = false;
-      break;
-    }
-    plan_nseg[stages] = nseg;
-    plan_seg[stages] = seg;
-    plan_n[stages + 1] = nseg * kk;
-    ++stages;
-  }
-  if (staged_ok) {
-    // Two ping-pong buffers of (idx, val) candidates per row batch.
-    const int64_t per_row = 2 * static_cast<int64_t>(plan_n[1]) * 8;
-    int64_t batch = kTopkTempBytes / per_row;
-    if (batch < 1) batch = 1;
-    if (batch > rows) batch = rows;
-    void* temp = nullptr;
-    if (cudaMallocAsync(&temp, static_cast<size_t>(batch * per_row), st) != cudaSuccess) {
-      cudaGetLastError();
-      temp = nullptr;
-    }
-    if (temp) {
-      int32_t* bi[2] = {static_cast<int32_t*>(temp), static_cast<int32_t*>(temp) + batch * plan_n[1]};
-      float* bv[2] = {reinterpret_cast<float*>(bi[1] + batch * plan_n[1]),
-                      reinterpret_cast<float*>(bi[1] + batch * plan_n[1]) + batch * plan_n[1]};
-      int rc = DSV32_OK;
-      for (int64_t r0 = 0; r0 < rows && rc == DSV32_OK; r0 += batch) {
-        const int64_t rb = (rows - r0 < batch) ? rows - r0 : batch;
-        // stage 0 reads the caller's rows (causal tail skipped), later stages the candidate lists
-        const float* in_v = scores ? scores + r0 * ld : nullptr;
-        const int32_t* in_c = cand_idx ? cand_idx + r0 * cand_ld : nullptr;
-        int64_t in_ld = ld, in_cld = cand_ld, off = idx_offset;
-        int in_cm = cm;
-        int64_t in_cs = causal_start;
-        for (int sidx = 0; sidx < stages && rc == DSV32_OK; ++sidx) {
-          const int b = sidx & 1;
-          dsv32::topk::RowParts pr = sidx == 0 ? p0 : no_parts;  // parts of this row batch
-          for (int j = 0; j < pr.n; ++j) {
-            pr.v[j] += r0 * pr.ld;
-            pr.id[j] += r0 * pr.ld;
-          }
-          rc = topk_reg_launch(in_v, rb, plan_n[sidx], in_ld, in_c, in_cld, off, kk, bi[b], bv[b], in_cm, in_cs, r0,
-                               plan_seg[sidx], plan_nseg[sidx], st, pr);
-          in_v = bv[b];
-          in_c = bi[b];
-          in_ld = in_cld = plan_n[sidx + 1];
-          off = 0;
-          in_cm = 0;
-          in_cs = 0;
+  const TopkPlan plan = topk_plan(nn, kk, parts != nullptr);
+  const int64_t batch = (plan.ok && workspace) ? std::min<int64_t>(rows, ws_bytes / plan.per_row) : 0;
+  if (batch >= 1) {
+    const int stages = plan.stages;
+    const int64_t slot = batch * plan.n[1];  // candidates per buffer
+    int32_t* bi[2] = {static_cast<int32_t*>(workspace), static_cast<int32_t*>(workspace) + slot};
+    float* bv[2] = {reinterpret_cast<float*>(bi[1] + slot), reinterpret_cast<float*>(bi[1] + slot) + slot};
+    for (int64_t r0 = 0; r0 < rows; r0 += batch) {
+      const int64_t rb = (rows - r0 < batch) ? rows - r0 : batch;
+      // stage 0 reads the caller's rows (causal tail skipped), later stages the candidate lists
+      const float* in_v = scores ? scores + r0 * ld : nullptr;
+      const int32_t* in_c = cand_idx ? cand_idx + r0 * cand_ld : nullptr;
+      int64_t in_ld = ld, in_cld = cand_ld, off = idx_offset;
+      int in_cm = cm;
+      int64_t in_cs = causal_start;
+      for (int sidx = 0; sidx < stages; ++sidx) {
+        const int b = sidx & 1;
+        dsv32::topk::RowParts pr = sidx == 0 ? p0 : no_parts;  // parts of this row batch
+        for (int j = 0; j < pr.n; ++j) {
+          pr.v[j] += r0 * pr.ld;
+          pr.id[j] += r0 * pr.ld;
         }
-        if (rc == DSV32_OK)
-          rc = topk_reg_launch(in_v, rb, plan_n[stages], in_ld, in_c, in_cld, off, kk, out_idx + r0 * k,
-                               out_val + r0 * k, in_cm, in_cs, r0, plan_n[stages], 1, st);
+        if (int rc = topk_reg_launch(in_v, rb, plan.n[sidx], in_ld, in_c, in_cld, off, kk, bi[b], bv[b], in_cm, in_cs,
+                                     r0, plan.seg[sidx], plan.nseg[sidx], st, pr))
+          return rc;
+        in_v = bv[b];
+        in_c = bi[b];
+        in_ld = in_cld = plan.n[sidx + 1];
+        off = 0;
+        in_cm = 0;
+        in_cs = 0;
       }
-      const cudaError_t fe = cudaFreeAsync(temp, st);
-      if (rc != DSV32_OK) return rc;
-      if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync");
-      return DSV32_OK;
+      if (int rc = topk_reg_launch(in_v, rb, plan.n[stages], in_ld, in_c, in_cld, off, kk, out_idx + r0 * k,
+                                   out_val + r0 * k, in_cm, in_cs, r0, plan.n[stages], 1, st))
+        return rc;
     }
+    return DSV32_OK;
   }
-  if (parts) return DSV32_ERR_UNSUPPORTED;  // the long-row kernel reads plain rows only
+  if (parts) {  // the long-row kernel reads plain rows only
+    t_last_error = plan.ok ? "dsv32_topk_parts: rows longer than 8192 positions need a workspace of "
+                                 "dsv32_topk_workspace_bytes() bytes"
+                           : "dsv32_topk_parts: no staged plan for these list lengths";
+    return DSV32_ERR_UNSUPPORTED;
+  }
   return launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rows), 1024, 0, st, "topk kernel launch", scores, ld, nn,
                 cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
 }
@@ -533,13 +587,14 @@ int dsv32_int8_gemm_noalloc(const int8_t* a, const float* a_s, const int8_t* b, 
   if (int st = device_setup(&dev, &info)) return st;
   GemmPlan plan = gemm_plan(m, n, k, info->num_sms, kNoAllocTilesCap, dsv32::gemm::slot_rows_for(m));
   uint8_t* ws = nullptr;
+  if (plan.split && plan.ws_bytes > kNoAllocScratchBytes) {
+    // The balanced schedule would not fit the static scratch: whole tiles per SM instead, which
+    // need no scratch (what dsv32_int8_gemm does without a workspace; same results up to fp32
+    // summation order).
+    plan.split = false;
+    plan.grid = static_cast<int>(plan.tiles < info->num_sms ? plan.tiles : info->num_sms);
+  }
   if (plan.split) {
-    if (plan.ws_bytes > kNoAllocScratchBytes) {
-      t_last_error = "dsv32_int8_gemm_noalloc: this problem needs " + std::to_string(plan.ws_bytes) +
-                     " bytes of scratch, the static scratch holds " + std::to_string(kNoAllocScratchBytes) +
-                     " (problems with fewer 128-row tiles than SMs fit up to m = 32); use dsv32_int8_gemm";
-      return DSV32_ERR_UNSUPPORTED;
-    }
     {
       // First call on this device (with it current): look up the array's device address once.
       std::lock_guard<std::mutex> lock(g_mu);
@@ -565,13 +620,21 @@ int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b,
 }
 
 int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
-                     int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, void* stream) {
-  return index_impl(q, w, k, k_s, out, batch, m, n, heads, dim, causal, start, stream);
+                     int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, int64_t k_ld,
+                     void* stream) {
+  return index_impl(q, w, k, k_s, out, batch, m, n, heads, dim, causal, start, k_ld, 1, stream);
+}
+
+int64_t dsv32_topk_workspace_bytes(int64_t rows, int64_t n, int64_t k, int nparts) {
+  if (nparts < 0 || nparts > dsv32::topk::kMaxParts) return -DSV32_ERR_INVALID_ARG;
+  return topk_ws_bytes(rows, n, k, nparts);
 }
 
 int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
-               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
-  return topk_impl(scores, rows, n, ld, cand_idx, cand_ld, idx_offset, k, out_idx, out_val, stream);
+               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* workspace,
+               int64_t workspace_bytes, void* stream) {
+  return topk_impl(scores, rows, n, ld, cand_idx, cand_ld, idx_offset, k, out_idx, out_val, workspace,
+                   workspace_bytes, stream);
 }
 
 int dsv32_device_alloc(int64_t bytes, void** ptr) {
@@ -613,7 +676,8 @@ int dsv32_ipc_close(void* ptr) {
 }
 
 int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
-                     int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* stream) {
+                     int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* workspace,
+                     int64_t workspace_bytes, void* stream) {
   if (!part_vals || !part_ids || nparts < 1 || nparts > dsv32::topk::kMaxParts) return DSV32_ERR_INVALID_ARG;
   if (rows < 1 || part_len < 1 || part_ld < part_len || k < 1 || k > nparts * part_len) return DSV32_ERR_INVALID_ARG;
   if (part_len % 16 != 0 || nparts * part_len > (1LL << 30)) return DSV32_ERR_UNSUPPORTED;
@@ -626,20 +690,28 @@ int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_i
   parts.ld = part_ld;
   parts.len = static_cast<int>(part_len);
   parts.n = nparts;
-  return topk_impl(nullptr, rows, nparts * part_len, part_ld, nullptr, 0, 0, k, out_idx, out_val, stream, 0, 0, &parts);
+  return topk_impl(nullptr, rows, nparts * part_len, part_ld, nullptr, 0, 0, k, out_idx, out_val, workspace,
+                   workspace_bytes, stream, 0, 0, &parts);
 }
 
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,
                           int64_t batch, int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start,
-                          int64_t topk, int64_t key_offset, int32_t* out_idx, float* out_val, void* stream) {
+                          int64_t k_ld, int scores_out, int64_t topk, int64_t key_offset, int32_t* out_idx,
+                          float* out_val, void* workspace, int64_t workspace_bytes, void* stream) {
   if (topk < 1 || topk > n) return DSV32_ERR_INVALID_ARG;
   if (!out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
-  if (int st = index_impl(q, w, k, k_s, scores, batch, m, n, heads, dim, causal, start, stream)) return st;
-  return topk_impl(scores, batch * m, n, n, nullptr, 0, key_offset, topk, out_idx, out_val, stream, causal ? m : 0,
-                   start);
+  if (workspace && (!aligned16(workspace) || workspace_bytes < 0)) return DSV32_ERR_INVALID_ARG;
+  // Without scores_out the masked tiles of causal rows stay unwritten: the selection never reads a
+  // causal row past its visible length.
+  if (int st = index_impl(q, w, k, k_s, scores, batch, m, n, heads, dim, causal, start, k_ld,
+                          (scores_out || !causal) ? 1 : 0, stream))
+    return st;
+  return topk_impl(scores, batch * m, n, n, nullptr, 0, key_offset, topk, out_idx, out_val, workspace,
+                   workspace_bytes, stream, causal ? m : 0, start);
 }
 
-int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s, void* stream) {
+int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s,
+                       const float* scale_mul, void* stream) {
   if (!x || !y || !s) return DSV32_ERR_INVALID_ARG;
   if (rows < 0) return DSV32_ERR_INVALID_ARG;
   if (x_dtype != DSV32_F32 && x_dtype != DSV32_BF16 && x_dtype != DSV32_F16) return DSV32_ERR_INVALID_ARG;
@@ -657,12 +729,12 @@ int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int
   const char* what = "rotate_quant_kernel launch";
   if (x_dtype == DSV32_F32)
     return launch(rotate_quant_kernel<float>, g, kRqThreads, 0, st, what, static_cast<const float*>(x), y, s, rows,
-                  rotate);
+                  rotate, scale_mul);
   if (x_dtype == DSV32_BF16)
     return launch(rotate_quant_kernel<__nv_bfloat16>, g, kRqThreads, 0, st, what,
-                  static_cast<const __nv_bfloat16*>(x), y, s, rows, rotate);
+                  static_cast<const __nv_bfloat16*>(x), y, s, rows, rotate, scale_mul);
   return launch(rotate_quant_kernel<__half>, g, kRqThreads, 0, st, what, static_cast<const __half*>(x), y, s, rows,
-                rotate);
+                rotate, scale_mul);
 }
 
 int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t* wq, float* ws, void* stream) {

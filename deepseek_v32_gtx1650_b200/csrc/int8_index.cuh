@@ -21,7 +21,11 @@
 //               into a 4-stage ring.
 //   warp 17     MMA issuer: D / 32 MMAs per key tile into one of two int32 TMEM accumulators.
 //   warp 18     writes -inf for the key tiles that no query of a unit can see (causal), which are
-//               neither loaded nor multiplied (the reference's tile skip, kernels.py:145-148).
+//               neither loaded nor multiplied (the reference's tile skip, kernels.py:145-148). With
+//               fill_masked == 0 (scores used only as the selection's scratch, whose causal rows are
+//               never read past their visible length) those tiles are left unwritten.
+// Keys and their scales of batch b start at key b * ks_ld (ks_ld >= N: a cache with spare capacity
+// is read in place).
 //
 // Per logit: relu and the int32 -> fp32 conversion in one saturating fp32 multiply of the raw bits
 // (relu_i32_x2m22, exact for |logit| <= D*128*128 <= 2^21, giving relu * 2^-22), then one fused
@@ -116,7 +120,8 @@ template <int H, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_index_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const float* __restrict__ w, const float* __restrict__ k_s, float* __restrict__ out, int M,
-                      int N, int causal, long long start, int tiles_per_chunk, int num_chunks, int units) {
+                      int N, int causal, long long start, int tiles_per_chunk, int num_chunks, int units,
+                      long long ks_ld, int fill_masked) {
   using C = Cfg<H, D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -251,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ -inf for invisible key tiles
     const int ft = lane;
     const bool vec4 = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
-    for (int r = 0;; ++r) {
+    for (int r = 0; fill_masked; ++r) {
       const int idx = unit_of_round(r, units);
       if (idx < 0) break;
       const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
@@ -304,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Per unit: this thread's key column, its k_s and output pointers, and per query the last
       // visible tile offset (so the per-tile work has no 64-bit arithmetic).
       const int n_base = wq * 32 + lane;
-      const float* ksp = k_s + static_cast<int64_t>(un.b) * N + n_base;
+      const float* ksp = k_s + static_cast<int64_t>(un.b) * ks_ld + n_base;
       float* outp[C::kQPerWarp];
       int lim[C::kQPerWarp];  // the key of tile offset t is visible to query q iff t <= lim[q]
 #pragma unroll

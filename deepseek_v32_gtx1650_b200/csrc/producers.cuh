@@ -10,6 +10,8 @@
 //   fp32 and fp64 round a tie apart, scales within 1e-5).
 //   Layout: 8 lanes per vector, 16 consecutive values per lane: stages of stride 1-8 stay in the
 //   lane's registers, strides 16, 32, 64 are lane shuffles (xor 1, 2, 4).
+//   With s_mul, s[r] = s_mul[r] * scale instead (the indexer folds its query scales into the head
+//   weights, bench_indexer_e2e.py:55, without a separate elementwise kernel).
 //
 // weight_quant: the GEMM's B operand (test_kernels.py:80-82, bench.py:43-44): per 128 x 128 block
 //   of W [N, K], s = max(amax, 1e-4) / 127 (an fp32 division), y = clamp(rint(x / s), -127, 127);
@@ -53,7 +55,8 @@ DSV32_DEV uint4 pack16(const uint32_t (&q)[16]) {
 
 template <typename T>
 __global__ void __launch_bounds__(kRqThreads, 4) rotate_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
-                                                                   float* __restrict__ s, int64_t rows, int rotate) {
+                                                                   float* __restrict__ s, int64_t rows, int rotate,
+                                                                   const float* __restrict__ s_mul) {
   constexpr int LPV = 8;          // lanes per vector
   constexpr int VPW = 32 / LPV;   // vectors per warp slot
   const int lane = threadIdx.x & 31;
@@ -122,7 +125,9 @@ __global__ void __launch_bounds__(kRqThreads, 4) rotate_quant_kernel(const T* __
       uint32_t q[16];
       aq_quant_lane<16>(v, sc, rc, q);
       __stcs(reinterpret_cast<uint4*>(y + row * 128 + sl * 16), pack16(q));
-      if (sl == 0) s[row] = sc;
+      // s_mul: the indexer's head weights, which take the per-vector query scale (w * qs,
+      // bench_indexer_e2e.py:55: one fp32 rounding, as the reference's product)
+      if (sl == 0) s[row] = s_mul ? __ldg(s_mul + row) * sc : sc;
     }
   }
 }

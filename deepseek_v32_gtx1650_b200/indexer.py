@@ -39,14 +39,13 @@ def indexer_step(q: torch.Tensor, w: torch.Tensor, cache: KeyCache, k_new: torch
     with head weights w [B, M, H] select the top-k of the cache's keys [0, length).
     Causal: query m is the token at position length - M + m and sees keys up to itself.
     Returns (idx int32 [B, M, topk], vals fp32 [B, M, topk]) (and the scores first when
-    return_scores). The query scales multiply w as in bench_indexer_e2e.py:55."""
+    return_scores). The query scales multiply w as in bench_indexer_e2e.py:55, inside the rotate +
+    quantise kernel; the cache's keys [0, length) are read in place (no copy of the cache)."""
     if k_new is not None:
         cache.append(k_new)
     B, M, H, D = q.shape
     N = cache.length
-    qq, qs = rotate_quant(q.contiguous())  # [B, M, H, 128] int8, [B, M, H]
-    w2 = (w * qs).contiguous()
-    k = cache.k[:, :N] if N == cache.k.shape[1] else cache.k[:, :N].contiguous()
-    k_s = cache.k_s[:, :N] if N == cache.k_s.shape[1] else cache.k_s[:, :N].contiguous()
-    return int8_index_topk(qq, w2, k, k_s, topk=min(topk, N), causal=causal, start=N - M,
-                           return_scores=return_scores)
+    # [B, M, H, 128] int8 and the head weights times the per-vector query scales [B, M, H]
+    qq, w2 = rotate_quant(q.contiguous(), scale_mul=w.float().contiguous())
+    return int8_index_topk(qq, w2, cache.k, cache.k_s, topk=min(topk, N), causal=causal, start=N - M,
+                           return_scores=return_scores, n_keys=N)

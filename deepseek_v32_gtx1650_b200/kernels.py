@@ -59,6 +59,25 @@ def _gemm_workspace(dev: torch.device, stream: int, M: int, N: int, K: int):
     return ws.data_ptr(), ws.numel()
 
 
+# Top-k workspace per (device, stream): scratch of the staged selection of rows longer than 8192 keys
+# (no initialisation needed). Grown on demand, so steady-state calls allocate nothing.
+_TOPK_WS: dict = {}
+
+
+def _topk_workspace(dev: torch.device, stream: int, rows: int, n: int, k: int, nparts: int = 0):
+    nbytes = int(_lib.load().dsv32_topk_workspace_bytes(rows, n, k, nparts))
+    if nbytes < 0:
+        _lib.check(-nbytes, "topk workspace")
+    if nbytes == 0:
+        return None, 0
+    key = (dev.index, stream)
+    ws = _TOPK_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _TOPK_WS[key] = ws
+    return ws.data_ptr(), ws.numel()
+
+
 def _require_cuda(*ts: torch.Tensor) -> None:
     for t in ts:
         if not t.is_cuda:
@@ -147,7 +166,7 @@ def int8_index(q, w, k, k_s, causal=False, start=0, block_q=None, block_n=None, 
     if B and M and Nk:
         with _OnDevice(q):
             _lib.check(_lib.load().dsv32_int8_index(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
-                                                    o.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start),
+                                                    o.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start), 0,
                                                     _stream(q)), "int8_index")
     return o
 
@@ -173,8 +192,10 @@ def select_topk(scores: torch.Tensor, k: int, idx_offset: int = 0, cand_idx: tor
         cp, cld = None, 0
     if rows:
         with _OnDevice(scores):
+            st = _stream(scores)
+            ws, wsb = _topk_workspace(scores.device, st, rows, n, k)
             _lib.check(_lib.load().dsv32_topk(scores.data_ptr(), rows, n, n, cp, cld, int(idx_offset), k,
-                                              idx.data_ptr(), vals.data_ptr(), _stream(scores)), "select_topk")
+                                              idx.data_ptr(), vals.data_ptr(), ws, wsb, st), "select_topk")
     return idx, vals
 
 
@@ -183,17 +204,23 @@ def _ptr_array(ptrs):
     return ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), arr
 
 
-def topk_parts_raw(val_ptrs, id_ptrs, rows: int, part_ld: int, part_len: int, k: int, device: torch.device):
+def topk_parts_raw(val_ptrs, id_ptrs, rows: int, part_ld: int, part_len: int, k: int, device: torch.device,
+                   workspace=None, out=None):
     """Top-k over rows that are the concatenation of len(val_ptrs) lists given as raw device
     addresses (list j of row r at val_ptrs[j] + 4 * r * part_ld, ids likewise), which may be other
-    GPUs' memory mapped with CUDA IPC. Returns (idx int32 [rows, k], vals fp32 [rows, k])."""
-    idx = torch.empty(rows, k, device=device, dtype=torch.int32)
-    vals = torch.empty(rows, k, device=device, dtype=torch.float32)
+    GPUs' memory mapped with CUDA IPC. workspace: (device address, bytes) reserved by the caller
+    (default: the per-stream top-k workspace); out: (idx, vals) tensors to write. Returns
+    (idx int32 [rows, k], vals fp32 [rows, k])."""
+    idx, vals = out if out is not None else (torch.empty(rows, k, device=device, dtype=torch.int32),
+                                             torch.empty(rows, k, device=device, dtype=torch.float32))
     pv, keep_v = _ptr_array(val_ptrs)
     pi, keep_i = _ptr_array(id_ptrs)
     with _OnDevice(idx):
+        st = _stream(idx)
+        ws, wsb = workspace if workspace is not None else _topk_workspace(device, st, rows, len(val_ptrs) * part_len,
+                                                                           k, len(val_ptrs))
         _lib.check(_lib.load().dsv32_topk_parts(pv, pi, len(val_ptrs), rows, part_ld, part_len, k, idx.data_ptr(),
-                                                vals.data_ptr(), _stream(idx)), "select_topk_parts")
+                                                vals.data_ptr(), ws, wsb, st), "select_topk_parts")
     return idx, vals
 
 
@@ -211,26 +238,37 @@ def select_topk_parts(vals_list, idx_list, k: int):
                           vals_list[0].device)
 
 
-def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_scores=True, key_offset=0):
+def _index_topk_launch(q, w, k, k_s, n_keys, scores, scores_out, topk, causal, start, key_offset, out_idx_ptr,
+                       out_val_ptr):
+    B, M, H, D = q.shape
+    lib = _lib.load()
+    with _OnDevice(q):
+        s = _stream(q)
+        ws, wsb = _topk_workspace(q.device, s, B * M, n_keys, topk)
+        _lib.check(lib.dsv32_int8_index_topk(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
+                                             scores.data_ptr(), B, M, n_keys, H, D, int(bool(causal)), int(start),
+                                             k.shape[1], int(bool(scores_out)), topk, int(key_offset), out_idx_ptr,
+                                             out_val_ptr, ws, wsb, s), "int8_index_topk")
+
+
+def int8_index_topk(q, w, k, k_s, topk=2048, causal=False, start=0, return_scores=True, key_offset=0, n_keys=None):
     """Indexer scores + per-query top-k in one call (the step bench_indexer_e2e.py:54-57,72-77 runs).
 
     Returns (scores [b, m, n], idx int32 [b, m, topk], vals fp32 [b, m, topk]), or (idx, vals) when
     return_scores is False. idx are key positions (+ key_offset), in increasing order per query;
-    see select_topk for the tie rule."""
-    B, M, H, D, Nk = _index_checks(q, w, k, k_s)
+    see select_topk for the tie rule. n_keys: score only the first n_keys keys of each batch of k / k_s
+    (a key cache [b, capacity, d] read in place); default all of them."""
+    B, M, H, D, cap = _index_checks(q, w, k, k_s)
+    Nk = cap if n_keys is None else int(n_keys)
+    assert 1 <= Nk <= cap, "n_keys must be in [1, k.shape[1]]"
     assert 1 <= topk <= Nk, "topk must be in [1, n]"
     _require_cuda(q, w, k, k_s)
     scores = torch.empty(B, M, Nk, device=q.device, dtype=torch.float32)
     idx = torch.empty(B, M, topk, device=q.device, dtype=torch.int32)
     vals = torch.empty(B, M, topk, device=q.device, dtype=torch.float32)
     if B and M:
-        lib = _lib.load()
-        with _OnDevice(q):
-            s = _stream(q)
-            _lib.check(lib.dsv32_int8_index_topk(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
-                                                 scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)), int(start),
-                                                 topk, int(key_offset), idx.data_ptr(), vals.data_ptr(), s),
-                       "int8_index_topk")
+        _index_topk_launch(q, w, k, k_s, Nk, scores, return_scores, topk, causal, start, key_offset, idx.data_ptr(),
+                           vals.data_ptr())
     return (scores, idx, vals) if return_scores else (idx, vals)
 
 
@@ -243,28 +281,31 @@ def int8_index_topk_into(q, w, k, k_s, out_idx_ptr: int, out_val_ptr: int, topk=
     _require_cuda(q, w, k, k_s)
     scores = torch.empty(B, M, Nk, device=q.device, dtype=torch.float32)
     if B and M:
-        with _OnDevice(q):
-            _lib.check(_lib.load().dsv32_int8_index_topk(q.data_ptr(), w.data_ptr(), k.data_ptr(), k_s.data_ptr(),
-                                                         scores.data_ptr(), B, M, Nk, H, D, int(bool(causal)),
-                                                         int(start), topk, int(key_offset), out_idx_ptr,
-                                                         out_val_ptr, _stream(q)), "int8_index_topk")
+        _index_topk_launch(q, w, k, k_s, Nk, scores, False, topk, causal, start, key_offset, out_idx_ptr,
+                           out_val_ptr)
 
 
-def rotate_quant(x: torch.Tensor, rotate: bool = True):
+def rotate_quant(x: torch.Tensor, rotate: bool = True, scale_mul: torch.Tensor | None = None):
     """The indexer's operand producer: x [..., 128] fp32/bf16/fp16 -> (int8 [..., 128], fp32 [...]).
     Each 128-vector is rotated by the Hadamard transform scaled by 128^-1/2 (rotate=True) and
     quantised with one scale per vector (hadamard_quant.py:63-103), in the row-major layout
-    int8_index reads."""
+    int8_index reads. scale_mul (fp32, shape x.shape[:-1]): the scales come back multiplied by it,
+    one fp32 rounding (the indexer's w * qs, bench_indexer_e2e.py:55)."""
     assert x.is_contiguous() and x.shape[-1] == GROUP, "rotate_quant works on 128-value vectors"
     assert x.dtype in _DT, f"rotate_quant supports float32/bfloat16/float16, got {x.dtype}"
     _require_cuda(x)
     rows = x.numel() // GROUP
+    if scale_mul is not None:
+        assert scale_mul.dtype == torch.float32 and scale_mul.is_contiguous()
+        assert scale_mul.shape == x.shape[:-1] and scale_mul.device == x.device
     y = torch.empty(x.shape, device=x.device, dtype=torch.int8)
     s = torch.empty(x.shape[:-1], device=x.device, dtype=torch.float32)
     if rows:
         with _OnDevice(x):
             _lib.check(_lib.load().dsv32_rotate_quant(x.data_ptr(), _DT[x.dtype], rows, int(bool(rotate)),
-                                                      y.data_ptr(), s.data_ptr(), _stream(x)), "rotate_quant")
+                                                      y.data_ptr(), s.data_ptr(),
+                                                      None if scale_mul is None else scale_mul.data_ptr(),
+                                                      _stream(x)), "rotate_quant")
     return y, s
 
 

@@ -104,8 +104,10 @@ class PeerLists:
     """This rank's top-k lists of `rows` rows (ids [rows, k] int32, then values [rows, k] fp32, in one
     cudaMalloc allocation) and every peer's, mapped into this process with CUDA IPC, so the merge
     kernel reads the other ranks' lists in place over NVLink. Built once per (rows, k, device, group)
-    by a collective (all ranks construct it together); released at exit. `usable` is False on every
-    rank if any rank could not allocate, export or map (the caller then exchanges through NCCL)."""
+    by a collective (all ranks construct it together); released at exit. The merge's top-k workspace
+    (rows of world * k candidates longer than one register pass are selected in stages) is reserved
+    here too, so a merge allocates nothing. `usable` is False on every rank if any rank could not
+    allocate, export or map (the caller then exchanges through NCCL)."""
 
     _cache: dict = {}
 
@@ -113,11 +115,19 @@ class PeerLists:
         lib = _lib.load()
         self.rows, self.k, self.world, self.rank = rows, k, dist.get_world_size(group), dist.get_rank(group)
         self.bases, self.opened, self.own = [], [], 0
+        self.ws, self.ws_arg = None, (None, 0)
         ok = True
         with torch.cuda.device(device):
+            nbytes = int(lib.dsv32_topk_workspace_bytes(rows // self.world, self.world * k, k, self.world))
+            if nbytes > 0:
+                try:
+                    self.ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+                    self.ws_arg = (self.ws.data_ptr(), nbytes)
+                except RuntimeError:
+                    ok = False
             base = ctypes.c_void_p()
             handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
-            if lib.dsv32_device_alloc(rows * k * 8, ctypes.byref(base)) == _lib.DSV32_OK:
+            if ok and lib.dsv32_device_alloc(rows * k * 8, ctypes.byref(base)) == _lib.DSV32_OK:
                 self.own = base.value
                 ok = lib.dsv32_ipc_export(base, handle) == _lib.DSV32_OK
             else:
@@ -159,6 +169,7 @@ class PeerLists:
         if self.own:
             lib.dsv32_device_free(ctypes.c_void_p(self.own))
             self.own = 0
+        self.ws, self.ws_arg = None, (None, 0)
 
     @classmethod
     def get(cls, rows: int, k: int, device: torch.device, group=None):
@@ -169,15 +180,30 @@ class PeerLists:
 
 
 def _p2p_usable(rows: int, k: int, world: int, device: torch.device, group=None) -> bool:
-    return (device.type == "cuda" and dist.get_backend(group) == "nccl" and 1 < world <= 16 and rows % world == 0
-            and k % 16 == 0)
+    """Whether the peer-memory merge applies: NCCL ranks on GPUs, rows that split evenly, lists of a
+    multiple of 16, and a selection plan for rows of world * k candidates read as lists (host-side
+    arithmetic, identical on every rank, so every rank takes the same path)."""
+    if not (device.type == "cuda" and dist.get_backend(group) == "nccl" and 1 < world <= 16 and rows % world == 0
+            and k % 16 == 0):
+        return False
+    return int(_lib.load().dsv32_topk_workspace_bytes(rows // world, world * k, k, world)) >= 0
+
+
+def _mark(events, name):
+    """Profiling hook: with a list, record a timing event on the current stream after a stage."""
+    if events is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events.append((name, ev))
 
 
 def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, causal: bool = False,
-                       start: int = 0, group=None):
+                       start: int = 0, group=None, events: list | None = None):
     """Key-range sharded indexer + top-k. q [B, M, H, D], w [B, M, H] replicated; k_local [B, n_r, D],
     k_s_local [B, n_r] this rank's keys starting at global key key_lo. Returns (idx int32 [B, M, topk],
-    vals fp32 [B, M, topk]) on every rank, identical to the single-GPU int8_index_topk."""
+    vals fp32 [B, M, topk]) on every rank, identical to the single-GPU int8_index_topk.
+    events: optional list; a (stage name, CUDA event) pair is appended after each stage (for
+    per-stage timing; the events must not be used inside a graph capture)."""
     B, M = q.shape[:2]
     assert k_local.shape[1] >= topk, "each key shard must hold at least topk keys"
     world = dist.get_world_size(group)
@@ -187,24 +213,30 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     if ex is None or not ex.usable:  # (usable is decided collectively: every rank takes the same path)
         idx, vals = K.int8_index_topk(q, w, k_local, k_s_local, topk=topk, causal=causal, start=lstart,
                                       return_scores=False, key_offset=key_lo)
+        _mark(events, "index+local_topk")
         midx, mval = merge_candidates(idx.view(rows, topk), vals.view(rows, topk), topk, group)
+        _mark(events, "nccl_exchange+merge")
         return midx.view(B, M, topk), mval.view(B, M, topk)
     # Peer-memory exchange: the local selection writes straight into this rank's mapped buffer, a
     # one-element all-reduce orders every rank's selection before any read, and the merge kernel
     # reads this rank's row block of every rank's lists in place over NVLink.
     K.int8_index_topk_into(q, w, k_local, k_s_local, ex.ids_ptr(ex.rank), ex.vals_ptr(ex.rank), topk=topk,
                            causal=causal, start=lstart, key_offset=key_lo)
+    _mark(events, "index+local_topk")
     dist.all_reduce(ex.flag, group=group)
+    _mark(events, "order_allreduce")
     r = rows // world
     r0 = ex.rank * r
     mi, mv = K.topk_parts_raw([ex.vals_ptr(j, r0) for j in range(world)], [ex.ids_ptr(j, r0) for j in range(world)],
-                              r, topk, topk, topk, q.device)
+                              r, topk, topk, topk, q.device, workspace=ex.ws_arg)
+    _mark(events, "merge_peer_lists")
     # Merged row blocks to every rank. A rank passes this point only after every rank's merge kernel
     # has run (they precede the all-gather on each stream), so the next call may overwrite the lists.
     out_i = torch.empty(rows, topk, dtype=torch.int32, device=q.device)
     out_b = torch.empty(rows, topk, dtype=torch.int32, device=q.device)
     dist.all_gather_into_tensor(out_i, mi, group=group)
     dist.all_gather_into_tensor(out_b, mv.view(torch.int32), group=group)
+    _mark(events, "allgather_rows")
     return out_i.view(B, M, topk), out_b.view(torch.float32).view(B, M, topk)
 
 

@@ -8,8 +8,10 @@
  *
  * Conventions shared by all entry points
  *  - All pointers are device pointers to contiguous row-major arrays, 16-byte aligned.
- *  - Outputs are caller-allocated; inputs are never written. Nothing here allocates device
- *    memory except the per-device launch set-up on first use (function attributes).
+ *  - Outputs and scratch are caller-allocated; inputs are never written. No compute entry point
+ *    allocates device memory: kernels that need scratch (the stream-K GEMM, the staged top-k of long
+ *    rows) take a caller workspace sized by a *_workspace_bytes() query. The only allocating calls
+ *    are dsv32_device_alloc / dsv32_ipc_open, which exist to allocate and map memory.
  *  - Status codes: DSV32_OK on success; DSV32_ERR_* otherwise (see dsv32_status_string()).
  *    Argument errors are detected before any launch. Kernels that time out on an internal
  *    wait report it through dsv32_device_status().
@@ -25,7 +27,7 @@
 extern "C" {
 #endif
 
-#define DSV32_ABI_VERSION 5
+#define DSV32_ABI_VERSION 6
 
 /* Status codes. */
 #define DSV32_OK 0
@@ -83,9 +85,10 @@ int dsv32_int8_gemm_partials(const int8_t* a, const float* a_s, const int8_t* b,
  *  - All calls share the one array: calls that may overlap on the GPU (other streams, other host
  *    threads) race and must be serialised by the caller.
  *  - Problems with at least one wave of 128-row tiles (one per SM) need no scratch and run at any
- *    size. Smaller problems spread their K blocks over all SMs through the scratch; those that
- *    would need more than 10 MiB (for example m = 128 with n = 7168) return DSV32_ERR_UNSUPPORTED,
- *    with the needed size in dsv32_last_error_message(). */
+ *    size. Smaller problems spread their K blocks over all SMs through the scratch; those whose
+ *    spread would need more than 10 MiB (for example m = 128 with n = 7168) run whole tiles per SM
+ *    instead, which needs no scratch (same results up to fp32 summation order, as dsv32_int8_gemm
+ *    without a workspace). */
 int dsv32_int8_gemm_noalloc(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c,
                             int c_dtype, int64_t m, int64_t n, int64_t k, void* stream);
 
@@ -95,9 +98,21 @@ int dsv32_int8_gemm_noalloc(const int8_t* a, const float* a_s, const int8_t* b, 
  * out [batch, m, n] fp32. (heads, dim) in {16, 32, 64} x {64, 128}.
  * out[b, i, j] = k_s[b, j] * sum_h w[b, i, h] * relu(q[b, i, h, :] . k[b, j, :]);
  * causal != 0: out = -inf where j > start + i (start may be negative: a key shard whose first
- * key lies past some queries' positions). */
+ * key lies past some queries' positions).
+ * k_ld: keys between the first keys of consecutive batches, for k (k_ld * dim bytes) and k_s (k_ld
+ * floats); 0 means n (contiguous). A key cache [batch, capacity, dim] holding n <= capacity valid
+ * keys is read in place with k_ld = capacity. */
 int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
-                     int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, void* stream);
+                     int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, int64_t k_ld,
+                     void* stream);
+
+/* Bytes of workspace the top-k selection of `rows` rows of n positions uses on the current device
+ * (0: none). nparts = 0 for dsv32_topk / dsv32_int8_index_topk rows, else the list count of a
+ * dsv32_topk_parts call (n = nparts * part_len). Rows of at most 8192 positions need none. Longer
+ * rows are selected in stages through the workspace, in row batches sized to whatever is passed
+ * (the returned size covers up to 256 MB of rows; less works down to one row's share). A negative
+ * value is -status: -DSV32_ERR_UNSUPPORTED when rows given as lists cannot be selected at all. */
+int64_t dsv32_topk_workspace_bytes(int64_t rows, int64_t n, int64_t k, int nparts);
 
 /* Top-k selection per row: replaces torch.topk(scores, k) on the indexer output
  * (test_kernels.py:125, bench_indexer_e2e.py:72-77).
@@ -105,19 +120,28 @@ int dsv32_int8_index(const int8_t* q, const float* w, const int8_t* k, const flo
  * value: lowest position first) and writes them in increasing position order:
  * out_idx [rows, k] int32, out_val [rows, k] fp32. The index written for position p is
  * cand_idx[r * cand_ld + p] when cand_idx is non-NULL (merging candidate lists), else p + idx_offset
- * (a shard's first global key). Requires 1 <= k <= n. */
+ * (a shard's first global key). Requires 1 <= k <= n.
+ * workspace: 16-byte aligned device scratch of workspace_bytes (dsv32_topk_workspace_bytes); its
+ * contents need no initialisation. NULL or smaller than one row's share: rows longer than 8192 are
+ * selected by a kernel that re-reads them from L2 instead (slower, no scratch). One workspace must
+ * not serve two launches that may run concurrently. */
 int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
-               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* stream);
+               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* workspace,
+               int64_t workspace_bytes, void* stream);
 
 /* Indexer + top-k in one call (bench_indexer_e2e.py:54-57,72-77): scores are written to the
- * caller's `scores` buffer [batch, m, n] fp32 (workspace; it also holds the full scores on return),
- * then the top `topk` keys of every (batch, query) row are selected as dsv32_topk does, with
- * index = key position + key_offset (a key shard's first global key; 0 for a whole cache).
- * With causal != 0 the selection does not re-read the masked tail of each row.
+ * caller's `scores` buffer [batch, m, n] fp32, then the top `topk` keys of every (batch, query) row
+ * are selected as dsv32_topk does, with index = key position + key_offset (a key shard's first
+ * global key; 0 for a whole cache). k_ld as in dsv32_int8_index.
+ * scores_out != 0: `scores` holds the full scores on return (-inf where masked). scores_out == 0:
+ * `scores` is scratch, and with causal != 0 its masked entries are left unwritten (the selection
+ * never reads a causal row past its visible length).
+ * workspace / workspace_bytes: the selection's scratch, as for dsv32_topk (rows = batch * m).
  * out_idx / out_val [batch, m, topk]. Requires 1 <= topk <= n. */
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,
                           int64_t batch, int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start,
-                          int64_t topk, int64_t key_offset, int32_t* out_idx, float* out_val, void* stream);
+                          int64_t k_ld, int scores_out, int64_t topk, int64_t key_offset, int32_t* out_idx,
+                          float* out_val, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Synchronises `device`, then reads and clears its kernel error word. *code = 0 if no kernel
  * gave up on an internal wait since the last call; else (kernel_id << 16) | site. Returns
@@ -135,8 +159,11 @@ const char* dsv32_last_error_message(void);
  * x_dtype (DSV32_F32 / DSV32_BF16 / DSV32_F16), 16-byte aligned. rotate != 0: each vector is
  * multiplied by the 128-point Hadamard matrix scaled by 128^-1/2 (butterfly form, fp32), then
  * quantised per vector: s[r] = max(amax, 1e-4) * fl32(1/127), y[r, :] = clamp(rint(x / s), -127, 127)
- * (hadamard_quant.py:63-81). rotate == 0: the quantisation alone. y int8 [rows, 128], s fp32 [rows]. */
-int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s, void* stream);
+ * (hadamard_quant.py:63-81). rotate == 0: the quantisation alone. y int8 [rows, 128], s fp32 [rows].
+ * scale_mul: NULL, or fp32 [rows]; then s[r] = scale_mul[r] * scale of vector r, one fp32 rounding
+ * (the indexer's head weights take the query scales this way, bench_indexer_e2e.py:55). */
+int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s,
+                       const float* scale_mul, void* stream);
 
 /* Weight block quantiser for the GEMM's B operand (test_kernels.py:80-82, bench.py:43-44; the
  * reference computes it inline in torch): w [n, k] of w_dtype, n % 128 == 0, k % 128 == 0, 16-byte
@@ -150,9 +177,12 @@ int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t*
  * their global key ids at part_ids[j] + r * part_ld. Selects as dsv32_topk does (ties: lower
  * position in the concatenation first) and writes the ids from the lists. The lists are read in
  * place and may live in other GPUs' memory (dsv32_ipc_open). 1 <= nparts <= 16, part_len % 16 == 0,
- * 1 <= k <= nparts * part_len. out_idx / out_val [rows, k]. */
+ * 1 <= k <= nparts * part_len. out_idx / out_val [rows, k]. Rows longer than 8192 positions need
+ * the workspace dsv32_topk_workspace_bytes(rows, nparts * part_len, k, nparts) reports (at least one
+ * row's share); without it they return DSV32_ERR_UNSUPPORTED before any launch. */
 int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
-                     int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* stream);
+                     int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* workspace,
+                     int64_t workspace_bytes, void* stream);
 
 /* Device memory another process on the node can map: cudaMalloc on the current device (the pointer
  * is the base of its allocation, as IPC export requires), and its release. */

@@ -38,7 +38,7 @@ def test_library_builds_and_exports_every_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.dsv32_abi_version() == 5
+    assert lib.dsv32_abi_version() == 6
     for code in range(6):
         assert lib.dsv32_status_string(code)
     assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")
@@ -56,12 +56,18 @@ def test_argument_validation_without_gpu():
     assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 0, 4, 100, 128, None, 0, None) == _lib.DSV32_ERR_UNSUPPORTED
     # bad dtype code, bad head configuration, bad top-k
     assert lib.dsv32_int8_gemm(fake, fake, fake, fake, fake, 7, 4, 128, 128, None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
-    assert lib.dsv32_int8_index(fake, fake, fake, fake, fake, 1, 4, 128, 48, 128, 0, 0, None) == \
+    assert lib.dsv32_int8_index(fake, fake, fake, fake, fake, 1, 4, 128, 48, 128, 0, 0, 0, None) == \
         _lib.DSV32_ERR_UNSUPPORTED
-    assert lib.dsv32_topk(fake, 4, 100, 100, None, 0, 0, 101, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    # a key batch stride shorter than the key count
+    assert lib.dsv32_int8_index(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 100, None) == \
+        _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk(fake, 4, 100, 100, None, 0, 0, 101, fake, fake, None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
+    # misaligned top-k workspace
+    assert lib.dsv32_topk(fake, 4, 100, 100, None, 0, 0, 10, fake, fake, ctypes.c_void_p(4096 + 8), 64, None) == \
+        _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_int8_gemm_workspace_bytes(4, 100, 128) == -_lib.DSV32_ERR_UNSUPPORTED
-    assert lib.dsv32_int8_index_topk(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 0, 0, fake, fake,
-                                     None) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_int8_index_topk(fake, fake, fake, fake, fake, 1, 4, 128, 64, 128, 0, 0, 0, 0, 0, 0, fake, fake,
+                                     None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
     # misaligned operand
     odd = ctypes.c_void_p(4096 + 4)
     assert lib.dsv32_int8_gemm(odd, fake, fake, fake, fake, 0, 4, 128, 128, None, 0, None) == _lib.DSV32_ERR_INVALID_ARG
@@ -82,13 +88,33 @@ def test_topk_parts_and_ipc_validation_without_gpu():
     P = ctypes.POINTER(ctypes.c_void_p)
     parts = ctypes.cast(ptrs, P)
     # no parts, too many parts, k larger than the concatenated row, lists not a multiple of 16 long
-    assert lib.dsv32_topk_parts(parts, parts, 0, 4, 64, 64, 8, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
-    assert lib.dsv32_topk_parts(parts, parts, 17, 4, 64, 64, 8, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
-    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 64, 129, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
-    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 40, 8, fake, fake, None) == _lib.DSV32_ERR_UNSUPPORTED
-    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 32, 64, 8, fake, fake, None) == _lib.DSV32_ERR_INVALID_ARG
+    z = (None, 0, None)  # no workspace, default stream
+    assert lib.dsv32_topk_parts(parts, parts, 0, 4, 64, 64, 8, fake, fake, *z) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts(parts, parts, 17, 4, 64, 64, 8, fake, fake, *z) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 64, 129, fake, fake, *z) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 40, 8, fake, fake, *z) == _lib.DSV32_ERR_UNSUPPORTED
+    assert lib.dsv32_topk_parts(parts, parts, 2, 4, 32, 64, 8, fake, fake, *z) == _lib.DSV32_ERR_INVALID_ARG
     # null arguments of the memory / IPC helpers
     assert lib.dsv32_device_alloc(0, ctypes.byref(ctypes.c_void_p())) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_ipc_export(None, fake) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_device_free(None) == _lib.DSV32_OK and lib.dsv32_ipc_close(None) == _lib.DSV32_OK
+
+
+def test_topk_workspace_query_without_gpu():
+    """The top-k workspace size is host arithmetic (no device needed): none for rows of at most 8192
+    positions, one staged plan's candidate buffers per row for longer rows, capped near 256 MB of
+    rows, and -UNSUPPORTED for list rows that cannot be selected."""
+    lib = _lib.load()
+    q = lib.dsv32_topk_workspace_bytes
+    assert q(4096, 4096, 2048, 0) == 0 and q(4096, 8192, 2048, 0) == 0
+    # 131072 keys, k = 2048: 16 segments -> 32768 candidates; two (id, value) buffers per row
+    per_row = 2 * 16 * 2048 * 8
+    assert q(4096, 131072, 2048, 0) == (256 << 20) // per_row * per_row
+    assert q(3, 131072, 2048, 0) == 3 * per_row
+    # 8 ranks' lists of 2048: 16384 candidates in 2 segments
+    assert q(512, 8 * 2048, 2048, 8) == 512 * 2 * 2 * 2048 * 8
+    # a segment shorter than k: no staged plan; plain rows fall back to the scratch-free kernel
+    assert q(4, 8193, 8000, 0) == 0
+    assert q(4, 8200, 8000, 2) == -_lib.DSV32_ERR_UNSUPPORTED
+    assert q(4, 100, 101, 0) == -_lib.DSV32_ERR_INVALID_ARG and q(4, 100, 10, 17) == -_lib.DSV32_ERR_INVALID_ARG

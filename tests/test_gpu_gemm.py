@@ -150,3 +150,42 @@ def test_gemm_stream_k_and_data_parallel_schedules_agree(M, N, K):
     assert torch.equal(outs[1], outs[2])
     assert torch.count_nonzero(ws[: 4 * 8 * 65536]) == 0  # counters left at zero
     assert_no_device_error()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 7168, 2048), (8, 7168, 2048), (16, 640, 512), (17, 2048, 7168),
+                                   (32, 7168, 2048), (33, 384, 1024), (48, 7168, 2048), (64, 256, 384),
+                                   (64, 38400, 256)])
+def test_gemm_decode_swapped_partials_bit_exact(M, N, K):
+    """m <= 64 runs the swapped kernel (weight rows on the UMMA M side, tokens padded to 16 / 32 / 64
+    on the N side): per-K-block int32 partials bit-exact, fp32 within 1e-5, with the stream-K
+    workspace (fewer weight tiles than SMs) and whole tiles per SM (n = 38400: 300 tiles)."""
+    a, a_s, b, b_s = workloads.gemm_inputs_uniform(M, N, K, seed=M * 3 + N)
+    c, p = D.int8_gemm_partials(a.to(DEV), a_s.to(DEV), b.to(DEV), b_s.to(DEV))
+    pr = O.int8_gemm_partials_ref(a.numpy(), b.numpy())
+    np.testing.assert_array_equal(npy(p).astype(np.int64), pr)
+    ref = O.int8_gemm_ref(a.numpy(), a_s.numpy(), b.numpy(), b_s.numpy())
+    assert rel_err(npy(c), ref) < 1e-5
+    for dt, tol in [(torch.float32, 1e-5), (torch.bfloat16, 1e-2), (torch.float16, 2e-3)]:
+        c2 = D.int8_gemm(a.to(DEV), a_s.to(DEV), b.to(DEV), b_s.to(DEV), out_dtype=dt)
+        assert rel_err(npy(c2.float()), ref) < tol
+    assert_no_device_error()
+
+
+def test_gemm_decode_swapped_without_workspace_and_repeated():
+    """The swapped kernel without a workspace (whole tiles per SM) equals the stream-K run up to fp32
+    summation order, and repeated stream-K calls on one workspace are bit-identical (the tile
+    counters are left at zero by every launch)."""
+    from deepseek_v32_gtx1650_b200 import _lib
+    M, N, K = 32, 7168, 2048
+    x, B, b_s = workloads.gemm_inputs(M, N, K, seed=4)
+    a, a_s = D.act_quant(x.to(DEV))
+    b, b_s = B.to(DEV), b_s.to(DEV)
+    outs = [D.int8_gemm(a, a_s, b, b_s) for _ in range(3)]
+    assert all(torch.equal(o, outs[0]) for o in outs)
+    c = torch.empty(M, N, device=DEV)
+    _lib.check(_lib.load().dsv32_int8_gemm(a.data_ptr(), a_s.data_ptr(), b.data_ptr(), b_s.data_ptr(), c.data_ptr(),
+                                           _lib.DSV32_F32, M, N, K, None, 0, torch.cuda.current_stream().cuda_stream),
+               "int8_gemm without workspace")
+    ref = O.int8_gemm_ref(npy(a), npy(a_s), B.numpy(), npy(b_s))
+    assert rel_err(npy(c), ref) < 1e-5 and rel_err(npy(outs[0]), ref) < 1e-5
+    assert_no_device_error()

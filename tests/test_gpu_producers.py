@@ -125,3 +125,16 @@ def test_indexer_step_matches_composition():
     ref = O.int8_index_ref(npy(qq), npy(w2), npy(kq), npy(ks), causal=True, start=n0, rows=rows)
     assert O.rel_err(npy(scores)[:, rows], ref) < 1e-5
     assert_no_device_error()
+
+
+def test_rotate_quant_scale_mul_is_w_times_qs():
+    """scale_mul folds the head weights into the query scales inside the producer: bit-identical to
+    the reference's separate w * qs (bench_indexer_e2e.py:55), and the int8 values are unchanged."""
+    g = torch.Generator().manual_seed(8)
+    q = torch.randn(2, 33, 64, 128, generator=g).to(DEV)
+    w = (torch.rand(2, 33, 64, generator=g) / 64).to(DEV)
+    qq, qs = D.rotate_quant(q)
+    qq2, ws = D.rotate_quant(q, scale_mul=w)
+    assert torch.equal(qq, qq2)
+    assert torch.equal(ws, w * qs)
+    assert_no_device_error()

@@ -161,3 +161,85 @@ def test_index_topk_causal_long_rows_batched():
     np.testing.assert_array_equal(npy(idx)[0][rows], ri)
     np.testing.assert_array_equal(npy(vals)[0][rows], rv)
     assert_no_device_error()
+
+
+def test_index_topk_baseline_long_full_size():
+    """BASELINE configs[4], long-context case on one GPU: 4096 queries x 131072 keys, causal with the
+    chunked-prefill start 126976, top-2048. Rows are selected in stages through the workspace.
+    Scores on 64 sampled rows (first and last included) are within 1e-5 of the float64 oracle with
+    exact -inf masks; the selection equals the deterministic top-k of the returned scores on those
+    rows and is a valid top-k of the float64 scores (tie-aware, at the kernel's tolerance where two
+    keys' fp32 scores order differently from their float64 ones). The indices-only call, which
+    leaves the masked tiles unwritten, selects the same keys."""
+    M, N, topk = 4096, 131072, 2048
+    start = N - M
+    q, w, k, ks = workloads.index_inputs(1, M, N, seed=0)
+    qd, wd, kd, ksd = q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV)
+    scores, idx, vals = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=start)
+    rows = sample_rows(M, 64, seed=4)
+    sc = npy(scores[0, torch.from_numpy(rows).to(DEV)])
+    del scores
+    ref = O.int8_index_ref(q.numpy(), w.numpy(), k.numpy(), ks.numpy(), causal=True, start=start, rows=rows,
+                           chunk=8)[0]
+    np.testing.assert_array_equal(np.isinf(sc), np.isinf(ref))
+    assert O.rel_err(sc, ref) < 1e-5
+    ri, rv = O.topk_ref(sc, topk)
+    sel = npy(idx)[0][rows]
+    np.testing.assert_array_equal(sel, ri)
+    np.testing.assert_array_equal(npy(vals)[0][rows], rv)
+    strict = [O.topk_valid(sel[j:j + 1], ref[j:j + 1], topk) for j in range(len(rows))]
+    banded = [s or _near_tie_ok(sel[j:j + 1], ref[j:j + 1], topk) for j, s in enumerate(strict)]
+    print(f"long config: {sum(strict)} of {len(rows)} sampled rows valid against float64 without the tie band")
+    assert all(banded)
+    idx2, vals2 = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=start, return_scores=False)
+    assert torch.equal(idx2, idx) and torch.equal(vals2, vals)
+    assert_no_device_error()
+
+
+def test_long_rows_without_workspace_use_the_scratch_free_kernel():
+    """dsv32_topk with no workspace selects rows longer than 8192 with the kernel that re-reads them
+    from L2 (no scratch); it must equal the staged selection."""
+    from deepseek_v32_gtx1650_b200 import _lib
+    rows, n, k = 5, 40000, 2048
+    s = _scores(rows, n, True, seed=17).to(DEV)
+    s[1, 5000:] = float("-inf")
+    gi, gv = D.select_topk(s, k)  # staged, with the per-stream workspace
+    oi = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+    ov = torch.empty(rows, k, device=DEV)
+    _lib.check(_lib.load().dsv32_topk(s.data_ptr(), rows, n, n, None, 0, 0, k, oi.data_ptr(), ov.data_ptr(), None, 0,
+                                      torch.cuda.current_stream().cuda_stream), "dsv32_topk without workspace")
+    assert torch.equal(oi, gi) and torch.equal(ov, gv)
+    assert_no_device_error()
+
+
+def test_index_topk_reads_key_cache_in_place():
+    """n_keys scores the first n_keys keys of a cache with spare capacity through the key batch
+    stride (no copy): identical to the call on the contiguous slice."""
+    B, M, cap, n, topk = 2, 96, 3000, 2100, 512
+    q, w, k, ks = workloads.index_inputs(B, M, cap, seed=13)
+    qd, wd, kd, ksd = q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV)
+    s1, i1, v1 = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=n - M, n_keys=n)
+    s2, i2, v2 = D.int8_index_topk(qd, wd, kd[:, :n].contiguous(), ksd[:, :n].contiguous(), topk=topk, causal=True,
+                                   start=n - M)
+    assert torch.equal(s1, s2) and torch.equal(i1, i2) and torch.equal(v1, v2)
+    assert_no_device_error()
+
+
+def test_steady_state_calls_allocate_no_device_memory():
+    """The library allocates nothing: after one call of each shape has filled the caller-side caches
+    (outputs, the top-k and GEMM workspaces), further decode and long-row calls leave the device's
+    free memory unchanged."""
+    qd, wd, kd, ksd = (t.to(DEV) for t in workloads.index_inputs(1, 4, 32768, seed=2))
+    ql, wl, kl, ksl = (t.to(DEV) for t in workloads.index_inputs(1, 64, 40000, seed=3))
+
+    def calls():
+        D.int8_index_topk(qd, wd, kd, ksd, topk=2048, return_scores=False)
+        D.int8_index_topk(ql, wl, kl, ksl, topk=2048, causal=True, start=40000 - 64, return_scores=False)
+        torch.cuda.synchronize()
+
+    calls()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        calls()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert_no_device_error()

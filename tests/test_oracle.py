@@ -141,3 +141,35 @@ def test_weight_quant_oracle_matches_reference_expressions(golden):
         q, s = O.weight_quant_ref(golden[f"wq_{wi}_w"])
         np.testing.assert_array_equal(s, golden[f"wq_{wi}_s"])
         np.testing.assert_array_equal(q, golden[f"wq_{wi}_q"])
+
+
+# ---------------------------------------------------------------- torch-on-CPU baselines
+def test_torch_baselines_match_reference(golden):
+    """oracle/reference_torch.py restates the reference's eager CPU paths (reference.py:8-82) that
+    bench.py times as the CPU baseline: act_quant_torch is bit-exact against the reference's golden
+    vectors; gemm_dequant_fp32 and the two eager indexers agree with the float64 goldens to fp32
+    accuracy; int_mm_unscaled is the exact unscaled integer product."""
+    from oracle import reference_torch as RT
+    for si in range(int(golden["aq_nshapes"])):
+        for rs in (0, 1):
+            x = torch.from_numpy(golden[f"aq_{si}_f32_x"])
+            y, s = RT.act_quant_torch(x, bool(rs))
+            np.testing.assert_array_equal(y.numpy(), golden[f"aq_{si}_f32_r{rs}_y"])
+            np.testing.assert_array_equal(s.numpy(), golden[f"aq_{si}_f32_r{rs}_s"])
+    for gi in range(int(golden["gm_ncases"])):
+        a, a_s, b, b_s = (torch.from_numpy(golden[f"gm_{gi}_{n}"]) for n in ("a", "as", "b", "bs"))
+        c = RT.gemm_dequant_fp32(a, a_s, RT.dequant_weight(b, b_s))
+        assert O.rel_err(c.double().numpy(), golden[f"gm_{gi}_c"]) < 1e-5
+    a, b = torch.from_numpy(golden["gm_3_a"]), torch.from_numpy(golden["gm_3_b"])
+    if a.shape[0] > 16:  # torch._int_mm wants m > 16 on CPU
+        p = RT.int_mm_unscaled(a, b.T.contiguous()).numpy().astype(np.int64)
+        np.testing.assert_array_equal(p, O.int8_gemm_partials_ref(a.numpy(), b.numpy()).sum(0))
+    for ii in range(int(golden["ix_ncases"])):
+        B, M, N, H, D, causal, start = golden[f"ix_{ii}_meta"].tolist()
+        if causal:
+            continue  # the reference's eager baselines score every key
+        q, w, k, ks = (torch.from_numpy(golden[f"ix_{ii}_{n}"]) for n in ("q", "w", "k", "ks"))
+        ref = golden[f"ix_{ii}_o"]
+        assert O.rel_err(RT.index_torch_fp32(q, w, k, ks).double().numpy(), ref) < 1e-5
+        if M * H > 16:
+            assert O.rel_err(RT.index_torch_int8(q, w, k, ks).double().numpy(), ref) < 1e-5

@@ -41,6 +41,7 @@ SIGNATURES = {
     "dsv32_rotate_quant": (_i32, [_p, _i32, _i64, _i32, _p, _p, _p, _p]),
     "dsv32_weight_quant": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p]),
     "dsv32_device_status": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint32)]),
+    "dsv32_set_wait_limit": (_i32, [_i64]),
     "dsv32_status_string": (ctypes.c_char_p, [_i32]),
     "dsv32_last_error_message": (ctypes.c_char_p, []),
     "dsv32_topk_parts": (_i32, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _i64, _i64, _i64, _i64, _p, _p, _p,

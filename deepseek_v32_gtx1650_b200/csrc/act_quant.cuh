@@ -169,7 +169,7 @@ DSV32_DEV float lane_absmax16(const uint32_t* w) {
 // EPL values of a group per lane (LPG = 128 / EPL lanes per group, 32 / LPG groups per warp slot),
 // read as EPL * sizeof(T) / 16 consecutive 16-byte vectors; UNROLL group slots per iteration.
 // kPackedAmax (16-bit input): the lane's amax on the packed words (absmax2) instead of per value.
-template <typename T, int EPL, int UNROLL, bool kPackedAmax = false>
+template <typename T, int EPL, int UNROLL, bool kPackedAmax = false, bool kPrefetch = false>
 __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
                                                         float* __restrict__ s, int64_t num_groups,
                                                         int round_scale) {
@@ -187,17 +187,32 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
   pdl_wait();
   pdl_launch_dependents();
 
-  for (int64_t base = warp * UNROLL; base < slots; base += nwarps * UNROLL) {
-    // All loads of the lane are issued before any is used; the raw vectors stay packed in
-    // registers until their group is processed.
-    uint4 raw[UNROLL][NV];
+  // The raw 16-byte vectors of UNROLL slots, loaded before any is used and kept packed in registers
+  // until their group is processed. kPrefetch: the next iteration's vectors are requested before
+  // this iteration's are processed (two sets in registers).
+  auto load = [&](int64_t b, uint4 (&dst)[UNROLL][NV]) {
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
-      const int64_t g = (base + u) * GPW + sub;
-      const bool valid = (base + u) < slots && g < num_groups;
+      const int64_t g = (b + u) * GPW + sub;
+      const bool valid = (b + u) < slots && g < num_groups;
       const uint4* src = reinterpret_cast<const uint4*>(x + g * 128 + sl * EPL);
 #pragma unroll
-      for (int j = 0; j < NV; ++j) raw[u][j] = valid ? __ldcs(src + j) : make_uint4(0u, 0u, 0u, 0u);
+      for (int j = 0; j < NV; ++j) dst[u][j] = valid ? __ldcs(src + j) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  const int64_t stride = nwarps * UNROLL;
+  uint4 next[UNROLL][NV];
+  if constexpr (kPrefetch) load(warp * UNROLL, next);
+  for (int64_t base = warp * UNROLL; base < slots; base += stride) {
+    uint4 raw[UNROLL][NV];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+        for (int j = 0; j < NV; ++j) raw[u][j] = next[u][j];
+      if (base + stride < slots) load(base + stride, next);
+    } else {
+      load(base, raw);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {

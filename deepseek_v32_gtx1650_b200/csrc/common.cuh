@@ -25,6 +25,11 @@
 // Layout: (kernel_id << 16) | site. Read and cleared by dsv32_device_status().
 __device__ unsigned int g_dsv32_device_error = 0;
 
+// Bound of the pipeline waits (mbar_wait), in SM clock cycles; set per device by
+// dsv32_set_wait_limit (failure-detection tests shorten it so that waits run out). Drain waits,
+// which let in-flight copies and MMAs land before a CTA exits, keep their own compile-time bound.
+__device__ long long g_dsv32_wait_limit = DSV32_WAIT_LIMIT_CYCLES;
+
 enum : unsigned int {
   KID_GEMM = 1,
   KID_INDEX = 2,
@@ -90,10 +95,11 @@ DSV32_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 DSV32_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
+  const long long limit = g_dsv32_wait_limit;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > DSV32_WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       record_device_error(code);
       return false;

@@ -176,6 +176,7 @@ int launch(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
 
 struct GemmPlan {
   int BN;
+  int ew = dsv32::gemm::kEpiWarps;  // epilogue warps of the 128-row kernel (8; 16 measured slower)
   int swap_mn;  // > 0: decode-sized m on the swapped kernel, tokens padded to this many
   int64_t tiles, units;
   int grid;
@@ -203,7 +204,11 @@ GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k, int num_sms,
   p.BN = (n % 256 == 0 && tiles256 >= num_sms && !p.swap_mn) ? 256 : 128;
   p.tiles = ((m + 127) / 128) * ((n + p.BN - 1) / p.BN);  // swapped: n / 128 weight tiles, one token tile
   p.units = p.tiles * (k / 128);
-  p.split = p.tiles < num_sms && p.tiles <= ws_tiles_cap;
+  // The swapped kernel streams each tile's weights through one CTA unless the tiles cover under a
+  // quarter of the SMs: whole tiles measured faster than spreading K blocks over every SM (m = 1, 8,
+  // 32, 64 at n = 7168, k = 2048: 8.6 / 8.8 / 10.6 / 12.9 us against 12.3 / 12.4 / 13.9 / 16.5 us),
+  // the partial-tile round trip through the workspace costing more than the SMs it brings in.
+  p.split = (p.swap_mn ? p.tiles * 4 < num_sms : p.tiles < num_sms) && p.tiles <= ws_tiles_cap;
   p.slot_rows = slot_rows;
   p.ws_tiles_cap = ws_tiles_cap;
   if (p.split) {
@@ -261,18 +266,16 @@ int gemm_launch(const GemmPlan& plan, const int8_t* a, const float* a_s, const i
     return DSV32_ERR_UNSUPPORTED;
   }
   const char* what = "int8_gemm_kernel launch";
-  if (plan.BN == 256) {
-    if (partials)
-      return launch(int8_gemm_kernel<256, true>, g, kThreads, Smem<256>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok,
-                    mi, ni, ki, partials, ws, cap, sr);
-    return launch(int8_gemm_kernel<256, false>, g, kThreads, Smem<256>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok, mi,
-                  ni, ki, static_cast<int32_t*>(nullptr), ws, cap, sr);
-  }
-  if (partials)
-    return launch(int8_gemm_kernel<128, true>, g, kThreads, Smem<128>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok, mi,
-                  ni, ki, partials, ws, cap, sr);
-  return launch(int8_gemm_kernel<128, false>, g, kThreads, Smem<128>::kAlloc, st, what, tmA, tmB, a_s, b_s, c, ok, mi,
-                ni, ki, static_cast<int32_t*>(nullptr), ws, cap, sr);
+#define DSV32_GEMM_CASE(BNN, EWW)                                                                                  \
+  if (plan.BN == BNN && plan.ew == EWW)                                                                            \
+    return partials ? launch(int8_gemm_kernel<BNN, true, EWW>, g, threads_for(EWW), Smem<BNN>::kAlloc, st, what,    \
+                             tmA, tmB, a_s, b_s, c, ok, mi, ni, ki, partials, ws, cap, sr)                         \
+                    : launch(int8_gemm_kernel<BNN, false, EWW>, g, threads_for(EWW), Smem<BNN>::kAlloc, st, what,   \
+                             tmA, tmB, a_s, b_s, c, ok, mi, ni, ki, static_cast<int32_t*>(nullptr), ws, cap, sr);
+  DSV32_GEMM_CASE(256, 8)
+  DSV32_GEMM_CASE(128, 8)
+#undef DSV32_GEMM_CASE
+  return DSV32_ERR_UNSUPPORTED;
 }
 
 int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype, int64_t m,
@@ -364,7 +367,7 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
 int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
                     int64_t idx_offset, int k, int32_t* out_idx, float* out_val, int causal_m, int64_t causal_start,
                     int64_t causal_row0, int seg_len, int nseg, cudaStream_t st,
-                    const dsv32::topk::RowParts& parts = dsv32::topk::RowParts{}) {
+                    const dsv32::topk::RowParts& parts = dsv32::topk::RowParts{}, const int* row_len = nullptr) {
   using namespace dsv32::topk;
   const int64_t grid = rows * nseg;
   if (grid > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
@@ -373,16 +376,24 @@ int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const in
   const char* what = "topk kernel launch";
   if (seg_len <= 256 * 4)
     return launch(topk_reg_kernel<256, 4>, g, 256, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx,
-                  out_val, causal_m, cs, cr0, seg_len, nseg, parts);
+                  out_val, causal_m, cs, cr0, seg_len, nseg, parts, row_len);
   if (seg_len <= 256 * 16)
     return launch(topk_reg_kernel<256, 16>, g, 256, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k,
-                  out_idx, out_val, causal_m, cs, cr0, seg_len, nseg, parts);
+                  out_idx, out_val, causal_m, cs, cr0, seg_len, nseg, parts, row_len);
   return launch(topk_reg_kernel<512, 16>, g, 512, 0, st, what, vals, ld, n, cand_idx, cand_ld, idx_offset, k, out_idx,
-                out_val, causal_m, cs, cr0, seg_len, nseg, parts);
+                out_val, causal_m, cs, cr0, seg_len, nseg, parts, row_len);
 }
 
 constexpr int kTopkRegMax = 512 * 16;                       // longest row a register pass holds
 constexpr int64_t kTopkPreferredBytes = int64_t(256) << 20;  // workspace the library asks for, at most
+
+// Long-row filter (topk_filter_kernel): plain rows longer than two register passes, k small enough
+// that a list of 3 k candidates fits one register pass, and at least as many rows as SMs (with fewer
+// rows the staged plan, which spreads each row's segments over several CTAs, is faster).
+constexpr int kTopkFilterMinN = 2 * kTopkRegMax;
+bool filter_shape(int64_t n, int64_t k) { return n > kTopkFilterMinN && 3 * k <= kTopkRegMax; }
+int filter_cap(int k) { return (3 * k + 15) / 16 * 16; }
+int64_t filter_per_row(int k) { return int64_t(filter_cap(k)) * 8 + 16; }
 
 // Stage plan for rows longer than one register pass: each row is cut into equal segments of at most
 // 8192 positions, every segment keeps its own top-k (a superset of the row's top-k within it), and the
@@ -425,12 +436,16 @@ int64_t topk_ws_bytes(int64_t rows, int64_t n, int64_t k, int nparts) {
   if (rows < 1 || n < 1 || k < 1 || k > n) return -DSV32_ERR_INVALID_ARG;
   if (n > (1LL << 31) - 1) return -DSV32_ERR_UNSUPPORTED;
   const TopkPlan p = topk_plan(static_cast<int>(n), static_cast<int>(k), nparts > 0);
-  if (!p.ok) return nparts > 0 ? -DSV32_ERR_UNSUPPORTED : 0;  // plain rows: the long-row kernel
-  if (p.per_row == 0) return 0;
-  int64_t batch = kTopkPreferredBytes / p.per_row;
+  if (!p.ok && nparts > 0) return -DSV32_ERR_UNSUPPORTED;
+  // plain rows: room for whichever of the staged plan and the filter the call takes (without either,
+  // the long-row kernel needs nothing)
+  int64_t per_row = p.ok ? p.per_row : 0;
+  if (nparts == 0 && filter_shape(n, k)) per_row = std::max(per_row, filter_per_row(static_cast<int>(k)));
+  if (per_row == 0) return 0;
+  int64_t batch = kTopkPreferredBytes / per_row;
   if (batch < 1) batch = 1;
   if (batch > rows) batch = rows;
-  return batch * p.per_row;
+  return batch * per_row;
 }
 
 // causal_m > 0: row r (= b * causal_m + m) has its scores past key causal_start + m masked to -inf
@@ -461,6 +476,33 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   if (n <= kTopkRegMax) {
     return topk_reg_launch(scores, rows, nn, ld, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, causal_start,
                            0, nn, 1, st, p0);
+  }
+  if (!parts && workspace && filter_shape(n, k) && rows >= info->num_sms &&
+      ws_bytes >= filter_per_row(kk)) {
+    // Filter, per row batch: candidate lists (ids, values, lengths) in the workspace, the register
+    // selection over each list, then the scratch-free kernel for the rows the lists do not cover.
+    const int cap = filter_cap(kk);
+    const int64_t fb = std::min<int64_t>(rows, ws_bytes / filter_per_row(kk));
+    int32_t* ci = static_cast<int32_t*>(workspace);
+    float* cv = reinterpret_cast<float*>(ci + fb * cap);
+    int* cn = reinterpret_cast<int*>(cv + fb * cap);
+    const long long cs = static_cast<long long>(causal_start);
+    for (int64_t r0 = 0; r0 < rows; r0 += fb) {
+      const int64_t rb = std::min<int64_t>(rows - r0, fb);
+      const int32_t* cin = cand_idx ? cand_idx + r0 * cand_ld : nullptr;
+      if (int rc = launch(topk_filter_kernel<kFilterThreads, kFilterItems>, static_cast<unsigned>(rb),
+                          kFilterThreads, 0, st, "topk filter kernel launch", scores + r0 * ld, ld, nn, cin, cand_ld,
+                          idx_offset, kk, cm, cs, static_cast<long long>(r0), ci, cv, cn, cap))
+        return rc;
+      if (int rc = topk_reg_launch(cv, rb, cap, cap, ci, cap, 0, kk, out_idx + r0 * k, out_val + r0 * k, 0, 0, 0, cap,
+                                   1, st, RowParts{}, cn))
+        return rc;
+      if (int rc = launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rb), 1024, 0, st, "topk kernel launch",
+                          scores + r0 * ld, ld, nn, cin, cand_ld, idx_offset, kk, out_idx + r0 * k, out_val + r0 * k,
+                          cm, cs, static_cast<long long>(r0), static_cast<const int*>(cn)))
+        return rc;
+    }
+    return DSV32_OK;
   }
   const TopkPlan plan = topk_plan(nn, kk, parts != nullptr);
   const int64_t batch = (plan.ok && workspace) ? std::min<int64_t>(rows, ws_bytes / plan.per_row) : 0;
@@ -507,7 +549,8 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
     return DSV32_ERR_UNSUPPORTED;
   }
   return launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rows), 1024, 0, st, "topk kernel launch", scores, ld, nn,
-                cand_idx, cand_ld, idx_offset, kk, out_idx, out_val);
+                cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, static_cast<long long>(causal_start), 0LL,
+                static_cast<const int*>(nullptr));
 }
 
 }  // namespace
@@ -760,6 +803,12 @@ int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t*
                   static_cast<const __nv_bfloat16*>(w), wq, ws, n, k);
   return launch(weight_quant_kernel<__half>, g, kWqThreads, 0, st, what, static_cast<const __half*>(w), wq, ws, n,
                 k);
+}
+
+int dsv32_set_wait_limit(int64_t cycles) {
+  const long long v = cycles > 0 ? static_cast<long long>(cycles) : DSV32_WAIT_LIMIT_CYCLES;
+  DSV32_CUDA_TRY(cudaMemcpyToSymbol(g_dsv32_wait_limit, &v, sizeof(v)));
+  return DSV32_OK;
 }
 
 int dsv32_device_status(int device, uint32_t* code) {

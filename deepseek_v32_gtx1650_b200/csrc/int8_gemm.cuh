@@ -37,17 +37,23 @@ namespace gemm {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = (kEpiWarps + 4) * 32;  // + one warpgroup: producer, MMA, 2 idle
-// Launch: 384 threads x 168 registers = 64512. setmaxnreg moves them to the epilogue:
-// 2 warpgroups x 128 x 216 + 1 warpgroup x 128 x 72 = 64512 (and per sub-partition
-// 216 + 216 + 72 = 504 <= 512).
-constexpr uint32_t kEpiRegs = 216;
-constexpr uint32_t kCtlRegs = 72;
-// setmaxnreg.inc draws on the registers the CTA was launched with, not on the SM's file: the
-// split must fit the launch total or the increasing warps wait forever.
-constexpr int kLaunchRegs = 168;  // __launch_bounds__(384, 1): 65536 / 384 rounded down to 8
-static_assert(kEpiRegs * kEpiWarps * 32 + kCtlRegs * 4 * 32 <= kThreads * kLaunchRegs,
+// Epilogue warps per CTA (EW = 8 or 16), the kernel's template parameter. The CTA is EW epilogue
+// warps plus one warpgroup (producer, MMA issuer, 2 idle).
+constexpr int kEpiWarps = 8;        // default
+constexpr int kMaxEpiWarps = 16;    // counters per tile in the workspace (either layout fits)
+__host__ __device__ constexpr int threads_for(int ew) { return (ew + 4) * 32; }
+constexpr int kThreads = threads_for(kEpiWarps);
+// setmaxnreg moves registers from the control warpgroup to the epilogue. It draws on the registers
+// the CTA was launched with (threads x registers per thread at launch, 65536 / threads rounded down
+// to 8), not on the SM's file: the split must fit that total or the increasing warps wait forever.
+//   EW = 8:  384 threads x 168 = 64512 >= 2 x 128 x 216 + 128 x 72   (per sub-partition 504 <= 512)
+//   EW = 16: 640 threads x  96 = 61440 >= 4 x 128 x 112 + 128 x 32   (per sub-partition 480 <= 512)
+__host__ __device__ constexpr uint32_t epi_regs(int ew) { return ew == 8 ? 216u : 112u; }
+__host__ __device__ constexpr uint32_t ctl_regs(int ew) { return ew == 8 ? 72u : 32u; }
+__host__ __device__ constexpr int launch_regs(int ew) { return (65536 / threads_for(ew)) & ~7; }
+static_assert(epi_regs(8) * 8 * 32 + ctl_regs(8) * 4 * 32 <= threads_for(8) * launch_regs(8),
+              "register split exceeds the launch allocation");
+static_assert(epi_regs(16) * 16 * 32 + ctl_regs(16) * 4 * 32 <= threads_for(16) * launch_regs(16),
               "register split exceeds the launch allocation");
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
@@ -71,13 +77,13 @@ struct Smem {
 
 enum : uint32_t { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
 
-// Workspace layout (bytes): [counters: tiles_cap x 8 epilogue warps int32; a fixed capacity per
+// Workspace layout (bytes): [counters: tiles_cap x 16 int32 (one per tile and epilogue warp); a fixed capacity per
 // workspace, so the counters never share bytes with slot data whatever the problem shape]
 // [2 * grid slots of slot_rows x BN fp32, column-major]. Slot 2c holds CTA c's first segment, slot
 // 2c+1 its last one; slot_rows = min(128, M rounded up to 32) (rows past M are never written).
 // The counters must be zero before the first launch; every completed launch leaves them zero.
 constexpr int64_t kMaxSplitTiles = 65536;  // counter capacity of caller-provided workspaces
-__host__ __device__ constexpr int64_t counter_bytes(int64_t tiles_cap) { return tiles_cap * kEpiWarps * 4; }
+__host__ __device__ constexpr int64_t counter_bytes(int64_t tiles_cap) { return tiles_cap * kMaxEpiWarps * 4; }
 __host__ __device__ inline int slot_rows_for(int64_t m) {
   return static_cast<int>(m >= kBM ? kBM : ((m + 31) / 32) * 32);
 }
@@ -187,14 +193,16 @@ DSV32_DEV void store_row(const float2 (&acc)[kCols / 2], void* C, uint32_t out_k
   }
 }
 
-template <int BN, bool kPartials>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, bool kPartials, int EW = kEpiWarps>
+__global__ void __launch_bounds__(threads_for(EW), 1)
     int8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ a_s, const float* __restrict__ b_s, void* __restrict__ C,
                      uint32_t out_kind, int M, int N, int K, int32_t* __restrict__ partials,
                      uint8_t* __restrict__ workspace, int ws_tiles_cap, int slot_rows) {
+  static_assert(EW == 8 || EW == 16, "8 or 16 epilogue warps");
   using L = Smem<BN>;
-  constexpr int kCols = BN / 2;  // columns per epilogue thread
+  constexpr int kCols = BN / (EW / 4);  // columns per epilogue thread (EW / 4 column parts)
+  constexpr int kProducer = EW, kMma = EW + 1;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -230,13 +238,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < kTB; ++b) {
       mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), kEpiWarps);
+      mbar_init(tempty_bar(b), EW);
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) tmem_alloc(smem_u32(tmem_slot), kTB * BN);
+  if (warp == kMma) tmem_alloc(smem_u32(tmem_slot), kTB * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -244,10 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();  // no global memory access before this point
   pdl_launch_dependents();
 
-  if (warp >= kEpiWarps) {
-    regs_dec<kCtlRegs>();
+  if (warp >= EW) {
+    regs_dec<ctl_regs(EW)>();
   }
-  if (warp == kProducerWarp) {
+  if (warp == kProducer) {
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
@@ -285,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain_wait(full_bar(stage), phase);
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kMma) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_i8(kBM, BN);
       int stage = 0;
@@ -323,11 +331,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(mma_done_bar);
       drain_wait(mma_done_bar, 0);
     }
-  } else if (warp < kEpiWarps) {
-    regs_inc<kEpiRegs>();
+  } else if (warp < EW) {
+    regs_inc<epi_regs(EW)>();
     // ------------------------------------------------------------ promotion epilogue
     const int wq = warp & 3;   // TMEM lane quarter
-    const int wh = warp >> 2;  // column half
+    const int wh = warp >> 2;  // column part (of EW / 4)
     const int r_local = wq * 32 + lane;  // row within the tile
     const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wh * kCols);
     int* counters = reinterpret_cast<int*>(workspace);
@@ -373,8 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t tb = t_lane + buf * BN;
         // TMEM reads are software-pipelined one chunk ahead; 32-column chunks when the 64
-        // accumulators of a BN=128 tile leave room for two of them, else 16 columns.
-        constexpr int kCW = (kCols <= 64) ? 32 : 16;
+        // accumulators of a BN=128 tile leave room for two of them, else 16 columns (always 16 with
+        // 16 epilogue warps, whose threads have 112 registers).
+        constexpr int kCW = (EW == 8 && kCols <= 64) ? 32 : 16;
         uint32_t ra[kCW], rb[kCW];
         tmem_ld_async<kCW>(tb, ra);
         tmem_wait_ld<kCW>(ra);
@@ -424,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int c_last = sch.cta_of(t_u0 + sch.KG - 1);
       int is_last = 0;
       if (lane == 0) {
-        int* ctr = counters + static_cast<int64_t>(tile) * kEpiWarps + warp;
+        int* ctr = counters + static_cast<int64_t>(tile) * kMaxEpiWarps + warp;
         const int prev = atomicAdd(ctr, 1);
         is_last = (prev == c_last - c_first);
         if (is_last) *ctr = 0;  // ready for the next launch
@@ -455,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kMmaWarp) {
+  if (warp == kMma) {
     __syncwarp();
     tmem_dealloc(tmem_base, kTB * BN);
   }

@@ -246,7 +246,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
                                                            float* __restrict__ out_val, int causal_m,
                                                            long long causal_start, long long causal_row0,
                                                            int seg_len, int nseg,
-                                                           const __grid_constant__ RowParts parts) {
+                                                           const __grid_constant__ RowParts parts,
+                                                           const int* __restrict__ row_len = nullptr) {
   constexpr int W = THREADS / 32;
   static_assert(ITEMS <= 32, "per-thread selection masks are 32-bit");
   __shared__ RegShared<THREADS> sh;
@@ -257,7 +258,18 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   const long long row = out_row / nseg;
   const int seg0 = static_cast<int>(out_row % nseg) * seg_len;
   const int n = min(seg_len, n_total - seg0);
-  const int valid = max(0, min(n, row_valid(row + causal_row0, n_total, causal_m, causal_start) - seg0));
+  // row_len (candidate lists of the long-row filter, nseg = 1): row r holds row_len[r] >= k
+  // candidates; a negative length marks a row finished elsewhere.
+  int rl = n_total;
+  if (row_len) {
+    pdl_wait();
+    rl = row_len[row];
+    if (rl < 0) {
+      pdl_launch_dependents();
+      return;
+    }
+  }
+  const int valid = max(0, min(min(n, rl), row_valid(row + causal_row0, n_total, causal_m, causal_start) - seg0));
   const int pos0 = tid * ITEMS;
   // This thread's ITEMS positions: their scores and (merge passes) candidate ids. The ids are only
   // needed at the end; the lambda recomputes their address there instead of holding it.
@@ -698,20 +710,28 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
 }
 
 // ---------------------------------------------------------------------------- long rows
+// Positions at or past the row's visible length (causal rows) are -inf without being read. With
+// row_state, only rows whose state is kRowFallback are selected (the others finished elsewhere).
+constexpr int kRowFallback = -2;
 template <int THREADS>
 __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restrict__ vals, long long ld, int n,
                                                             const int32_t* __restrict__ cand_idx, long long cand_ld,
                                                             long long idx_offset, int k, int32_t* __restrict__ out_idx,
-                                                            float* __restrict__ out_val) {
+                                                            float* __restrict__ out_val, int causal_m,
+                                                            long long causal_start, long long causal_row0,
+                                                            const int* __restrict__ row_state) {
   __shared__ SelShared sh;
   int parity = 0;
   const long long row = blockIdx.x;
   const float* v = vals + row * ld;
   pdl_wait();
   pdl_launch_dependents();
+  if (row_state && row_state[row] != kRowFallback) return;
+  const int valid = row_valid(row + causal_row0, n, causal_m, causal_start);
+  auto key_at = [&](int i) { return i < valid ? fkey(__ldg(v + i)) : kNegInfKey; };
   int n_above = 0, n_ninf = 0;
   for (int i = threadIdx.x; i < n; i += THREADS) {
-    const uint32_t kk = fkey(__ldg(v + i));
+    const uint32_t kk = key_at(i);
     n_above += kk > kNegInfKey ? 1 : 0;
     n_ninf += kk == kNegInfKey ? 1 : 0;
   }
@@ -726,7 +746,7 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
     const uint32_t floor_key = (above >= k) ? kNegInfKey + 1u : 0u;
     uint32_t mn = 0xFFFFFFFFu, mx = 0u;
     for (int i = threadIdx.x; i < n; i += THREADS) {
-      const uint32_t kk = fkey(__ldg(v + i));
+      const uint32_t kk = key_at(i);
       mn = kk >= floor_key ? min(mn, kk) : mn;
       mx = kk >= floor_key ? max(mx, kk) : mx;
     }
@@ -741,7 +761,7 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
       __syncthreads();
       const int ns = shift - d;
       for (int i = threadIdx.x; i < n; i += THREADS) {
-        const uint32_t kk = fkey(__ldg(v + i));
+        const uint32_t kk = key_at(i);
         if (kk >= floor_key && prefix_match(kk, prefix, shift)) atomicAdd(&sh.hist[(kk >> ns) & (nbins - 1)], 1);
       }
       __syncthreads();
@@ -759,7 +779,7 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
   const int p1 = min(n, p0 + chunk);
   int gt = 0, eq = 0;
   for (int pos = p0; pos < p1; ++pos) {
-    const uint32_t kk = fkey(__ldg(v + pos));
+    const uint32_t kk = key_at(pos);
     gt += kk > T;
     eq += kk == T;
   }
@@ -771,7 +791,7 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
   float* ov = out_val + row * k;
   int e = eq_before;
   for (int pos = p0; pos < p1; ++pos) {
-    const float x = __ldg(v + pos);
+    const float x = pos < valid ? __ldg(v + pos) : -INFINITY;
     const uint32_t kk = fkey(x);
     bool sel = kk > T;
     if (kk == T) {
@@ -784,6 +804,178 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
       ++o;
     }
   }
+}
+
+// ---------------------------------------------------------------------------- long rows: filter
+// Rows much longer than one register pass (the long-context indexer: 131072 keys) are reduced to a
+// short candidate list in one read: a sample of the row gives a threshold T whose expected count of
+// keys >= T is about 1.5 k; one pass over the row writes every key >= T, in position order, with its
+// id, to the row's candidate list (at most `cap` = 3 k entries); the register kernel then selects the
+// k largest of the list (row_len = its length). Every key >= the row's k-th largest is in the list
+// whenever the list holds at least k keys, so the selection, ties included, equals the one over the
+// whole row. A row whose list would hold fewer than k keys or more than cap (a sample far from the
+// row's distribution, masked or negative-NaN keys among the k largest, at most k visible keys) is
+// marked kRowFallback and selected by topk_gmem_kernel instead. One CTA per row.
+constexpr int kFilterThreads = 512;
+constexpr int kFilterItems = 16;
+
+struct FilterShared {
+  int hist[1 << kRegBits];
+  int scan[32];
+  uint32_t prefix;
+  int krem, total;
+};
+
+// The c-th largest (1-based) key held by the block (ITEMS per thread; key 0 = no key), for
+// 1 <= c <= number of keys: up to three 11-bit histogram passes over the keys matching the prefix.
+template <int THREADS, int ITEMS>
+DSV32_DEV uint32_t block_kth_key(const uint32_t (&key)[ITEMS], int c, FilterShared& sh) {
+  uint32_t prefix = 0;
+  int shift = 32;
+  while (shift > 0) {
+    const int d = min(kRegBits, shift);
+    const int nbins = 1 << d;
+    const int ns = shift - d;
+    for (int i = threadIdx.x; i < nbins; i += THREADS) sh.hist[i] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i)
+      if (key[i] != 0u && prefix_match(key[i], prefix, shift)) atomicAdd(&sh.hist[(key[i] >> ns) & (nbins - 1)], 1);
+    __syncthreads();
+    const int per = (nbins + THREADS - 1) / THREADS;  // consecutive bins per thread, descending
+    int local = 0;
+    for (int j = 0; j < per; ++j) {
+      const int bin = nbins - 1 - (threadIdx.x * per + j);
+      if (bin >= 0) local += sh.hist[bin];
+    }
+    const int before = excl_scan_once<THREADS>(local, sh.scan);
+    if (before < c && c <= before + local) {
+      int acc = before;
+      for (int j = 0; j < per; ++j) {
+        const int bin = nbins - 1 - (threadIdx.x * per + j);
+        const int cnt = sh.hist[bin];
+        if (acc + cnt >= c) {
+          sh.prefix = prefix | (uint32_t(bin) << ns);
+          sh.krem = c - acc;
+          break;
+        }
+        acc += cnt;
+      }
+    }
+    __syncthreads();
+    prefix = sh.prefix;
+    c = sh.krem;
+    shift = ns;
+    __syncthreads();  // the next pass clears the histogram the scan above read
+  }
+  return prefix;
+}
+
+// Keys of ITEMS consecutive positions p .. p + ITEMS - 1 of a row (0 past `valid`).
+template <int ITEMS>
+DSV32_DEV void load_keys(const float* v, int p, int valid, uint32_t (&key)[ITEMS]) {
+  if ((reinterpret_cast<uintptr_t>(v + p) & 15u) == 0 && p + ITEMS <= valid) {
+#pragma unroll
+    for (int i = 0; i < ITEMS; i += 4) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(v + p + i));
+      key[i] = fkey(f.x);
+      key[i + 1] = fkey(f.y);
+      key[i + 2] = fkey(f.z);
+      key[i + 3] = fkey(f.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) key[i] = (p + i < valid) ? fkey(__ldg(v + p + i)) : 0u;
+  }
+}
+
+// Input row r of the batch: vals[r * ld .. + n) (positions past its causal visible length are -inf and
+// never read; causal row index r + causal_row0), candidate ids cand_in[r * cand_in_ld + p] or
+// p + idx_offset. Output: the row's list in cand_idx / cand_val[r * cap ..], its length in cand_n[r]
+// (kRowFallback when the list does not apply).
+template <int THREADS, int ITEMS>
+__global__ void __launch_bounds__(THREADS, 2)
+    topk_filter_kernel(const float* __restrict__ vals, long long ld, int n, const int32_t* __restrict__ cand_in,
+                       long long cand_in_ld, long long idx_offset, int k, int causal_m, long long causal_start,
+                       long long causal_row0, int32_t* __restrict__ cand_idx, float* __restrict__ cand_val,
+                       int* __restrict__ cand_n, int cap) {
+  constexpr int SPAN = THREADS * ITEMS;
+  __shared__ FilterShared sh;
+  const long long r = blockIdx.x;
+  const int tid = threadIdx.x;
+  const float* v = vals + r * ld;
+  const int32_t* cin = cand_in ? cand_in + r * cand_in_ld : nullptr;
+  const int valid = row_valid(r + causal_row0, n, causal_m, causal_start);
+  pdl_wait();
+  pdl_launch_dependents();
+  if (valid <= k) {  // the k outputs include masked positions: the general selection handles them
+    if (tid == 0) cand_n[r] = kRowFallback;
+    return;
+  }
+  // 1. Sample: thread t reads ITEMS consecutive positions at t * stride (the whole visible row when it
+  //    is at most SPAN long).
+  const int stride = max(ITEMS, (valid / THREADS) & ~(ITEMS - 1));
+  uint32_t key[ITEMS];
+  load_keys<ITEMS>(v, tid * stride, valid, key);
+  // Sampled positions (s_n) and keys (present: a negative NaN with all bits set reads as key 0 and is
+  // left out of the sample; the filter pass below still finds it like any other key).
+  int s_n = 0, present = 0;
+  {
+    int pos = max(0, min(ITEMS, valid - tid * stride)), have = 0;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) have += key[i] != 0u ? 1 : 0;
+    const int packed = __reduce_add_sync(0xffffffffu, (pos << 16) | have);  // ITEMS * 32 < 2^16
+    if ((tid & 31) == 0) sh.scan[tid >> 5] = packed;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) {
+      s_n += sh.scan[w] >> 16;
+      present += sh.scan[w] & 0xFFFF;
+    }
+    __syncthreads();
+  }
+  // 2. Threshold: the c-th largest sampled key, c scaled so that about 1.5 k keys of the row reach it
+  //    (exactly the k-th largest when the sample is the whole row).
+  long long c_ll = (s_n >= valid) ? k : (3LL * k * s_n + 2LL * valid - 1) / (2LL * valid);
+  if (c_ll < 1) c_ll = 1;
+  if (c_ll > present) c_ll = present;
+  if (present == 0) {
+    if (tid == 0) cand_n[r] = kRowFallback;
+    return;
+  }
+  const uint32_t T = block_kth_key<THREADS, ITEMS>(key, static_cast<int>(c_ll), sh);
+  if (T <= kNegInfKey) {  // -inf or negative NaN among the candidates: the general selection
+    if (tid == 0) cand_n[r] = kRowFallback;
+    return;
+  }
+  // 3. Ordered compaction of every key >= T, SPAN positions per round.
+  int32_t* ci = cand_idx + r * cap;
+  float* cv = cand_val + r * cap;
+  int running = 0;
+  for (int base = 0; base < valid; base += SPAN) {
+    const int p = base + tid * ITEMS;
+    load_keys<ITEMS>(v, p, valid, key);
+    uint32_t mask = 0;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) mask |= (key[i] >= T && key[i] != 0u) ? (1u << i) : 0u;
+    const int cnt = __popc(mask);
+    const int off = excl_scan_once<THREADS>(cnt, sh.scan);
+    if (tid == THREADS - 1) sh.total = off + cnt;
+    int o = running + off;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+      if (mask & (1u << i)) {
+        if (o < cap) {
+          ci[o] = cin ? cin[p + i] : static_cast<int32_t>(p + i + idx_offset);
+          cv[o] = fkey_inv(key[i]);
+        }
+        ++o;
+      }
+    }
+    __syncthreads();
+    running += sh.total;
+  }
+  if (tid == 0) cand_n[r] = (running >= k && running <= cap) ? running : kRowFallback;
 }
 
 }  // namespace topk

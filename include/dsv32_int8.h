@@ -148,6 +148,14 @@ int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, cons
  * DSV32_ERR_DEVICE_TIMEOUT when *code != 0. */
 int dsv32_device_status(int device, uint32_t* code);
 
+/* Bound, in SM clock cycles, after which a kernel gives up on an internal pipeline wait (a TMA load
+ * or MMA that never completes), records (kernel_id << 16) | site for dsv32_device_status(), lets its
+ * issued copies and MMAs land and returns; for the current device, for launches that follow.
+ * cycles <= 0 restores the default (2e9, about a second). Failure-detection tests set a few hundred
+ * cycles so that ordinary waits run out; the context stays usable. Not for use while kernels of the
+ * library run on the device. */
+int dsv32_set_wait_limit(int64_t cycles);
+
 /* Human-readable text for a status code (static storage). */
 const char* dsv32_status_string(int status);
 

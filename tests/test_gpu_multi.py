@@ -28,9 +28,9 @@ def _worker(rank, world, port, q):
         import deepseek_v32_gtx1650_b200 as D
         from deepseek_v32_gtx1650_b200 import sharded as S, workloads as W
         dev = torch.device("cuda", rank)
-        N, k = 16384, 2048
+        k = 2048
 
-        def index_case(M, seed):
+        def index_case(M, seed, N=16384):
             start = N - M
             q_, w, keys, ks = W.index_inputs(1, M, N, seed=seed)
             lo, hi = S.shard_range(N, world, rank)
@@ -40,8 +40,10 @@ def _worker(rank, world, port, q):
                                        start=start, return_scores=False)
             return torch.equal(idx, gi) and torch.equal(vals, gv)
 
-        # 256 rows: peer-memory exchange (twice: the mapped lists are reused), 255 rows: NCCL all-gather
-        ok_index = index_case(256, 11) and index_case(256, 12) and index_case(255, 13)
+        # 256 rows: peer-memory exchange (twice: the mapped lists are reused), 255 rows: NCCL all-gather;
+        # 65536 keys: each rank's 32768-key rows take the long-row filter before the merge
+        ok_index = (index_case(256, 11) and index_case(256, 12) and index_case(255, 13)
+                    and index_case(256, 14, N=65536))
         a, a_s, b, b_s = W.gemm_inputs_uniform(256, 256 * world, 1024, seed=5)
         blo, bhi = S.shard_range(b.shape[0], world, rank)
         c_loc = S.sharded_int8_gemm(a.to(dev), a_s.to(dev), b[blo:bhi].contiguous().to(dev),

@@ -243,3 +243,64 @@ def test_steady_state_calls_allocate_no_device_memory():
         calls()
     assert torch.cuda.mem_get_info()[0] == free0
     assert_no_device_error()
+
+
+@pytest.mark.parametrize("n,k,ties", [(20000, 2048, False), (40000, 2048, True), (65536, 1000, False),
+                                      (131072, 2048, True), (17000, 2730, False)])
+def test_long_rows_filter_equals_oracle(n, k, ties):
+    """Rows longer than two register passes, at least one per SM (160 rows): each row is reduced to the
+    keys at or above a sampled threshold, in position order, then selected in one register pass. The
+    selection equals the oracle's deterministic top-k, values and ties included."""
+    rows = 160
+    s = _scores(rows, n, ties, seed=n + k).to(DEV)
+    s[3, n // 2:] = float("-inf")      # a row with a long masked tail
+    s[4, : n - k] = float("-inf")      # exactly k values above -inf
+    s[5, 10] = float("inf")
+    idx, vals = D.select_topk(s, k)
+    pick = [0, 3, 4, 5, 77, rows - 1]
+    ri, rv = O.topk_ref(npy(s)[pick], k)
+    np.testing.assert_array_equal(npy(idx)[pick], ri)
+    np.testing.assert_array_equal(npy(vals)[pick], rv)
+    assert_no_device_error()
+
+
+def test_long_rows_filter_fallbacks():
+    """Rows on which the sampled threshold misjudges the row (large values only at positions the sample
+    skips, so the candidate list overflows; or only at sampled positions, so it holds fewer than k keys)
+    and rows with masked or negative-NaN keys among the k largest are selected by the scratch-free
+    kernel instead: every row still equals the oracle."""
+    rows, n, k = 160, 20000, 2048
+    g = torch.Generator().manual_seed(3)
+    s = torch.rand(rows, n, generator=g)
+    pos = torch.arange(n)
+    sampled = (pos < 512 * 32) & ((pos % 32) < 16)  # thread t samples [32 t, 32 t + 16) for n = 20000
+    big = torch.rand(rows, n, generator=g) + 10.0
+    s[0] = torch.where(~sampled, big[0], s[0])                 # large values the sample never sees
+    s[1] = torch.where(sampled, big[1], s[1])                  # the sample sees only large values
+    s[2, 100:] = float("-inf")                                 # few visible values
+    s[3, ::2] = torch.tensor(float("nan")).neg()               # negative NaNs everywhere
+    sd = s.to(DEV)
+    idx, vals = D.select_topk(sd, k)
+    pick = [0, 1, 2, 3, 50, rows - 1]
+    ri, rv = O.topk_ref(s.numpy()[pick], k)
+    np.testing.assert_array_equal(npy(idx)[pick], ri)
+    np.testing.assert_array_equal(npy(vals)[pick].view(np.int32), rv.astype(np.float32).view(np.int32))
+    assert_no_device_error()
+
+
+def test_index_topk_causal_long_rows_filter():
+    """The fused indexer + top-k on causal rows longer than two register passes (256 queries over 40000
+    keys): the filter skips each row's masked tail (left unwritten when the scores are scratch) and the
+    selection equals the deterministic top-k of the returned scores."""
+    B, M, N, topk = 1, 256, 40000, 2048
+    start = N - M
+    q, w, k, ks = workloads.index_inputs(B, M, N, seed=31)
+    qd, wd, kd, ksd = q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV)
+    scores, idx, vals = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=start)
+    rows = [0, 1, 100, 255]
+    ri, rv = O.topk_ref(npy(scores)[0][rows], topk)
+    np.testing.assert_array_equal(npy(idx)[0][rows], ri)
+    np.testing.assert_array_equal(npy(vals)[0][rows], rv)
+    idx2, vals2 = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=start, return_scores=False)
+    assert torch.equal(idx2, idx) and torch.equal(vals2, vals)
+    assert_no_device_error()

@@ -107,11 +107,65 @@ DSV32_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag
   }
 }
 
+// ---------------------------------------------------------------- thread-block clusters
+// The address of the same shared-memory location in CTA `rank` of this CTA's cluster.
+DSV32_DEV uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+DSV32_DEV void cluster_store(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster; the writes this thread made before it (to
+// that CTA's shared memory included) are visible to a cluster-scope acquire of the phase.
+DSV32_DEV void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+DSV32_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Every thread of every CTA of the cluster arrives and waits (release / acquire): at kernel start it
+// orders barrier initialisation before any remote access, at the end it keeps every CTA alive until
+// the others are done with its shared memory.
+DSV32_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Same wait, made warp-uniform: every lane polls, and the warp proceeds only if all
 // lanes saw the phase complete. Required before .sync.aligned tcgen05 instructions.
 DSV32_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int code) {
   bool ok = mbar_wait(bar, parity, abort_flag, code);
   return __all_sync(0xffffffffu, ok);
+}
+
+// mbar_wait with cluster-scope acquire (for phases completed by another CTA's remote arrive), bounded
+// the same way.
+DSV32_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  const long long limit = g_dsv32_wait_limit;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > limit) {
+      *abort_flag = 1;
+      record_device_error(code);
+      return false;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- TMA

@@ -93,6 +93,12 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<32, true>, gemm::SwapSmem<32>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, false>, gemm::SwapSmem<64>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, true>, gemm::SwapSmem<64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<16, false, 2>, gemm::SwapSmem<16, 2>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<16, true, 2>, gemm::SwapSmem<16, 2>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<32, false, 2>, gemm::SwapSmem<32, 2>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<32, true, 2>, gemm::SwapSmem<32, 2>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, false, 2>, gemm::SwapSmem<64, 2>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, true, 2>, gemm::SwapSmem<64, 2>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128>, index::Cfg<64, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128>, index::Cfg<32, 128>::kAlloc));
       DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128>, index::Cfg<16, 128>::kAlloc));
@@ -174,10 +180,34 @@ int launch(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
   return launch_check(what);
 }
 
+// launch() with the grid cut into clusters of `cluster` CTAs along x (grid a multiple of it).
+template <typename... KArgs, typename... Args>
+int launch_clusters(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                    const char* what, unsigned cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return launch_check(what);
+}
+
 struct GemmPlan {
   int BN;
   int ew = dsv32::gemm::kEpiWarps;  // epilogue warps of the 128-row kernel (8; 16 measured slower)
   int swap_mn;  // > 0: decode-sized m on the swapped kernel, tokens padded to this many
+  int pair = 1;  // 2: swapped kernel with a two-CTA cluster per tile, each CTA half of the K blocks
   int64_t tiles, units;
   int grid;
   bool split;
@@ -219,6 +249,13 @@ GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k, int num_sms,
     p.grid = static_cast<int>(p.tiles < num_sms ? p.tiles : num_sms);
     p.ws_bytes = 0;
   }
+  // Swapped kernel with whole tiles on at most half of the SMs: a CTA pair per tile, each streaming
+  // half of the K blocks (one SM streams its tile's weights at ~50 GB/s, so the tile count sets the
+  // bandwidth), the halves combined through the first CTA's shared memory (no workspace).
+  if (p.swap_mn && !p.split && p.tiles * 2 <= num_sms && k / 128 >= 2) {
+    p.pair = 2;
+    p.grid = static_cast<int>(2 * p.tiles);
+  }
   return p;
 }
 
@@ -253,12 +290,18 @@ int gemm_launch(const GemmPlan& plan, const int8_t* a, const float* a_s, const i
   const unsigned g = static_cast<unsigned>(plan.grid);
   if (plan.swap_mn) {
     const char* sw = "int8_gemm_swap_kernel launch";
-#define DSV32_SWAP_CASE(MN)                                                                                      \
-  if (plan.swap_mn == MN)                                                                                        \
+    int32_t* const no_p = nullptr;
+#define DSV32_SWAP_CASE(MN)                                                                                       \
+  if (plan.swap_mn == MN && plan.pair == 1)                                                                       \
     return partials ? launch(int8_gemm_swap_kernel<MN, true>, g, kSwThreads, SwapSmem<MN>::kAlloc, st, sw, tmA, tmB, \
-                             a_s, b_s, c, ok, mi, ni, ki, partials, ws, cap)                                     \
-                    : launch(int8_gemm_swap_kernel<MN, false>, g, kSwThreads, SwapSmem<MN>::kAlloc, st, sw, tmA,  \
-                             tmB, a_s, b_s, c, ok, mi, ni, ki, static_cast<int32_t*>(nullptr), ws, cap);
+                             a_s, b_s, c, ok, mi, ni, ki, partials, ws, cap)                                      \
+                    : launch(int8_gemm_swap_kernel<MN, false>, g, kSwThreads, SwapSmem<MN>::kAlloc, st, sw, tmA,   \
+                             tmB, a_s, b_s, c, ok, mi, ni, ki, no_p, ws, cap);                                    \
+  if (plan.swap_mn == MN && plan.pair == 2)                                                                       \
+    return partials ? launch_clusters(int8_gemm_swap_kernel<MN, true, 2>, g, kSwThreads, SwapSmem<MN, 2>::kAlloc,  \
+                                      st, sw, 2u, tmA, tmB, a_s, b_s, c, ok, mi, ni, ki, partials, ws, cap)       \
+                    : launch_clusters(int8_gemm_swap_kernel<MN, false, 2>, g, kSwThreads, SwapSmem<MN, 2>::kAlloc, \
+                                      st, sw, 2u, tmA, tmB, a_s, b_s, c, ok, mi, ni, ki, no_p, ws, cap);
     DSV32_SWAP_CASE(16)
     DSV32_SWAP_CASE(32)
     DSV32_SWAP_CASE(64)

@@ -15,10 +15,11 @@
 //               zero-filled by TMA) of each K block into an 8-stage ring.
 //   warp 5      MMA issuer: per K block, 4 x tcgen05.mma.kind::i8 (M = 128, N = MN, K = 32) into one
 //               of kTB TMEM accumulators.
-//   warps 0-3   promotion epilogue: warp w owns TMEM lanes 32w..32w+31 (weight rows). Per K block the
-//               per-token scales a_s[:, kb] * b_s[tile, kb] are formed once per warp (lane j holds
-//               token j's) and read back from shared memory as broadcasts; the int32 partials are
-//               converted exactly and accumulated in fp32 with packed FMAs.
+//   warps 0-3   promotion epilogue: warp w owns TMEM lanes 32w..32w+31 (weight rows). The per-token
+//               scales a_s[:, kb] * b_s[tile, kb] of 16 K blocks at a time are loaded with all loads
+//               in flight (lane j: token j), staged in the warp's shared memory and read back as
+//               broadcasts; the int32 partials are converted exactly and accumulated in fp32 with
+//               packed FMAs.
 //
 // Schedule: stream-K over (tile, K block) units exactly as int8_gemm_kernel (Sched / SegIter): every
 // CTA gets the same number of K blocks; partial tiles go through workspace slots of 128 x MN fp32
@@ -36,20 +37,26 @@ constexpr int kSwProducerWarp = kSwEpiWarps;
 constexpr int kSwMmaWarp = kSwEpiWarps + 1;
 constexpr int kSwMaxM = 64;  // largest m this path serves
 
-template <int MN>
+constexpr int kSwScKb = 16;  // K blocks of token scales staged per warp at a time
+
+// kPair = 2: a cluster of two CTAs per tile, each with half of the K blocks; the second pushes its fp32
+// partial into the first's shared memory (kOffRecv, [MN][128] fp32) and arrives on the first's
+// recv barrier of the same epilogue warp.
+template <int MN, int kPair = 1>
 struct SwapSmem {
   static_assert(MN == 16 || MN == 32 || MN == 64, "token tile of 16, 32 or 64 rows");
-  static constexpr int kStages = 8;
+  static constexpr int kStages = (MN == 64 && kPair == 2) ? 6 : 8;
   static constexpr int kB = kBM * kBK;           // weight tile bytes (UMMA M side)
   static constexpr int kA = MN * kBK;            // token tile bytes (UMMA N side), a multiple of 1024
   static constexpr int kTB = 256 / MN > 8 ? 8 : 256 / MN;  // TMEM accumulators of MN columns
   static constexpr int kTmemCols = (MN * kTB < 32) ? 32 : MN * kTB;  // a power of two >= 32
   static constexpr int kOffB = 0;
   static constexpr int kOffA = kOffB + kStages * kB;
-  static constexpr int kOffSc = kOffA + kStages * kA;  // per epilogue warp: MN scales
-  static constexpr int kOffBar = kOffSc + kSwEpiWarps * MN * 4;
-  // full[kStages], empty[kStages], tfull[kTB], tempty[kTB], mma_done
-  static constexpr int kNumBars = 2 * kStages + 2 * kTB + 1;
+  static constexpr int kOffSc = kOffA + kStages * kA;  // per epilogue warp: kSwScKb x MN scales
+  static constexpr int kOffRecv = kOffSc + kSwEpiWarps * kSwScKb * MN * 4;
+  static constexpr int kOffBar = kOffRecv + (kPair == 2 ? kBM * MN * 4 : 0);
+  // full[kStages], empty[kStages], tfull[kTB], tempty[kTB], mma_done, recv[kSwEpiWarps]
+  static constexpr int kNumBars = 2 * kStages + 2 * kTB + 1 + kSwEpiWarps;
   static constexpr int kOffTmem = kOffBar + 8 * kNumBars;
   static constexpr int kOffAbort = kOffTmem + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -96,13 +103,37 @@ DSV32_DEV void store_col(const float (&acc)[MN], void* C, uint32_t out_kind, int
   }
 }
 
-template <int MN, bool kPartials>
+// This CTA's segments: the stream-K / whole-tile schedule (SegIter), or with kPair = 2 the single
+// segment of a CTA pair: tile blockIdx.x / 2, the first or second half of its K blocks by cluster rank
+// (blockIdx.x % 2 for a 1-D grid of two-CTA clusters).
+template <int kPair>
+struct SwapIter {
+  SegIter inner;
+  bool used = false;
+  DSV32_DEV SwapIter(const Sched& s) : inner(s) {}
+  DSV32_DEV bool next(int& tile, int& kb0, int& kb1, bool& first) {
+    if constexpr (kPair == 1) {
+      return inner.next(tile, kb0, kb1, first);
+    } else {
+      if (used) return false;
+      used = true;
+      const int half = (inner.s.KG + 1) / 2;
+      tile = blockIdx.x / 2;
+      kb0 = (blockIdx.x & 1) ? half : 0;
+      kb1 = (blockIdx.x & 1) ? inner.s.KG : half;
+      first = true;
+      return true;
+    }
+  }
+};
+
+template <int MN, bool kPartials, int kPair = 1>
 __global__ void __launch_bounds__(kSwThreads, 1)
     int8_gemm_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const float* __restrict__ a_s, const float* __restrict__ b_s, void* __restrict__ C,
                           uint32_t out_kind, int M, int N, int K, int32_t* __restrict__ partials,
                           uint8_t* __restrict__ workspace, int ws_tiles_cap) {
-  using L = SwapSmem<MN>;
+  using L = SwapSmem<MN, kPair>;
   constexpr int kStages = L::kStages;
   constexpr int kTB = L::kTB;
   extern __shared__ uint8_t smem_raw[];
@@ -118,6 +149,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
   auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * kStages + b); };
   auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * kStages + kTB + b); };
   const uint32_t mma_done_bar = bar0 + 8u * (2 * kStages + 2 * kTB);
+  auto recv_bar = [&](int w) { return bar0 + 8u * (2 * kStages + 2 * kTB + 1 + w); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffTmem);
 
@@ -129,7 +161,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
   sch.num_tiles = sch.num_n;
   sch.grid = gridDim.x;
   sch.U = static_cast<long long>(sch.num_tiles) * sch.KG;
-  sch.split = workspace != nullptr;
+  sch.split = kPair == 1 && workspace != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -141,6 +173,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       mbar_init(tempty_bar(b), kSwEpiWarps);
     }
     mbar_init(mma_done_bar, 1);
+    for (int w = 0; w < kSwEpiWarps; ++w) mbar_init(recv_bar(w), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -148,6 +181,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if constexpr (kPair == 2) cluster_sync();  // the partner's barriers exist before any remote arrive
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // no global memory access before this point
   pdl_launch_dependents();
@@ -160,7 +194,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      SegIter it(sch);
+      SwapIter<kPair> it(sch);
       int tile, kb0, kb1;
       bool first;
       while (ok && it.next(tile, kb0, kb1, first)) {
@@ -195,7 +229,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       uint32_t phase = 0;
       uint32_t u = 0;  // K blocks multiplied by this CTA (selects the TMEM buffer)
       bool ok = true;
-      SegIter it(sch);
+      SwapIter<kPair> it(sch);
       int tile, kb0, kb1;
       bool first;
       while (ok && it.next(tile, kb0, kb1, first)) {
@@ -230,7 +264,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     // ------------------------------------------------------------ promotion epilogue (warps 0-3)
     const int r_local = warp * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem_base + (uint32_t(warp * 32) << 16);
-    float* sc_w = reinterpret_cast<float*>(smem + L::kOffSc) + warp * MN;  // this warp's token scales
+    float* sc_w = reinterpret_cast<float*>(smem + L::kOffSc) + warp * kSwScKb * MN;  // this warp's scales
     int* counters = reinterpret_cast<int*>(workspace);
     float* slots = workspace ? reinterpret_cast<float*>(workspace + counter_bytes(ws_tiles_cap)) : nullptr;
     constexpr int64_t kSlotFloats = static_cast<int64_t>(kBM) * MN;
@@ -240,7 +274,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       for (int b = 0; b < kTB; ++b) mbar_arrive(tempty_bar(b));  // every accumulator starts free
     }
     uint32_t u = 0;
-    SegIter it(sch);
+    SwapIter<kPair> it(sch);
     int tile, kb0, kb1;
     bool first_seg;
     while (ok && it.next(tile, kb0, kb1, first_seg)) {
@@ -249,23 +283,32 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       float acc[MN];
 #pragma unroll
       for (int j = 0; j < MN; ++j) acc[j] = 0.f;
-      // token scales of the next K block: lane j holds a_s[j, kb] (tokens past M read as 0)
+      // token j's scale of K block kb (tokens past M read as 0)
       auto token_scale = [&](int kb, int j) {
         return j < M ? __ldg(a_s + static_cast<int64_t>(j) * sch.KG + kb) : 0.f;
       };
-      float as0 = token_scale(kb0, lane), as1 = MN > 32 ? token_scale(kb0, lane + 32) : 0.f;
-      float sb = __ldg(bs_row + kb0);
       for (int kb = kb0; kb < kb1; ++kb, ++u) {
         const uint32_t buf = u % kTB;
-        // publish this K block's per-token scales, then prefetch the next block's
-        __syncwarp();
-        if (lane < MN) sc_w[lane] = as0 * sb;
-        if (MN > 32) sc_w[lane + 32] = as1 * sb;
-        __syncwarp();
-        if (kb + 1 < kb1) {
-          as0 = token_scale(kb + 1, lane);
-          if (MN > 32) as1 = token_scale(kb + 1, lane + 32);
-          sb = __ldg(bs_row + kb + 1);
+        const int ci = (kb - kb0) % kSwScKb;  // K block within the staged chunk
+        if (ci == 0) {
+          // Stage the per-token scales a_s[j, kb'] * b_s[tile, kb'] of the next kSwScKb K blocks (lane
+          // j: tokens j and j + 32): every load of the chunk is in flight at once, one L2 round trip
+          // per chunk instead of one per K block.
+          const int nkb = min(kSwScKb, kb1 - kb);
+          float bsv[kSwScKb], av0[kSwScKb], av1[kSwScKb];
+#pragma unroll
+          for (int i = 0; i < kSwScKb; ++i) {
+            bsv[i] = i < nkb ? __ldg(bs_row + kb + i) : 0.f;
+            av0[i] = i < nkb ? token_scale(kb + i, lane) : 0.f;
+            av1[i] = (MN > 32 && i < nkb) ? token_scale(kb + i, lane + 32) : 0.f;
+          }
+          __syncwarp();  // the previous chunk's broadcasts are read
+#pragma unroll
+          for (int i = 0; i < kSwScKb; ++i) {
+            if (lane < MN) sc_w[i * MN + lane] = av0[i] * bsv[i];
+            if (MN > 32) sc_w[i * MN + lane + 32] = av1[i] * bsv[i];
+          }
+          __syncwarp();
         }
         if (!mbar_wait_warp(tfull_bar(buf), (u / kTB) & 1u, abort_flag, (KID_GEMM << 16) | 14)) {
           ok = false;
@@ -282,7 +325,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           for (int j = 0; j < MN; ++j)
             if (j < M) partials[(static_cast<int64_t>(kb) * M + j) * N + n] = static_cast<int32_t>(r[j]);
         }
-        const float4* sc4 = reinterpret_cast<const float4*>(sc_w);
+        const float4* sc4 = reinterpret_cast<const float4*>(sc_w + ci * MN);
 #pragma unroll
         for (int j4 = 0; j4 < MN / 4; ++j4) {
           const float4 s4 = sc4[j4];  // same address across the warp: broadcast
@@ -300,6 +343,28 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       }
       if (!ok) break;
 
+      if constexpr (kPair == 2) {
+        // CTA pair: the second CTA pushes this warp's 32 rows x MN partial (the second half of K) into
+        // the first CTA's receive buffer and arrives on its barrier for this warp; the first adds it
+        // to its own (first half + second half: deterministic) and stores.
+        float* recv = reinterpret_cast<float*>(smem + L::kOffRecv);
+        if (blockIdx.x & 1) {
+          const uint32_t dst = cluster_map(smem_u32(recv), 0);
+#pragma unroll
+          for (int j = 0; j < MN; ++j) cluster_store(dst + 4u * static_cast<uint32_t>(j * kBM + r_local), acc[j]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(cluster_map(recv_bar(warp), 0));
+        } else {
+          if (!mbar_wait_cluster(recv_bar(warp), 0, abort_flag, (KID_GEMM << 16) | 15)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int j = 0; j < MN; ++j) acc[j] += recv[j * kBM + r_local];
+          store_col<MN>(acc, C, out_kind, M, N, n);
+        }
+        continue;
+      }
       if (kb0 == 0 && kb1 == sch.KG) {  // a whole tile: store directly
         store_col<MN>(acc, C, out_kind, M, N, n);
         continue;
@@ -347,6 +412,9 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     __syncwarp();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
+  // The first CTA of a pair stays until the second has finished writing into its shared memory (every
+  // path of both CTAs reaches this point: all their waits are bounded).
+  if constexpr (kPair == 2) cluster_sync();
 }
 
 }  // namespace gemm

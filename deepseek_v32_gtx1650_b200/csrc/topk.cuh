@@ -872,20 +872,22 @@ DSV32_DEV uint32_t block_kth_key(const uint32_t (&key)[ITEMS], int c, FilterShar
 }
 
 // Keys of ITEMS consecutive positions p .. p + ITEMS - 1 of a row (0 past `valid`).
+// The raw bits of ITEMS consecutive positions p .. p + ITEMS - 1 of a row; all ones past `valid` (whose
+// key, fkey, is 0: no key).
 template <int ITEMS>
-DSV32_DEV void load_keys(const float* v, int p, int valid, uint32_t (&key)[ITEMS]) {
+DSV32_DEV void load_bits(const float* v, int p, int valid, uint32_t (&bits)[ITEMS]) {
   if ((reinterpret_cast<uintptr_t>(v + p) & 15u) == 0 && p + ITEMS <= valid) {
 #pragma unroll
     for (int i = 0; i < ITEMS; i += 4) {
-      const float4 f = __ldg(reinterpret_cast<const float4*>(v + p + i));
-      key[i] = fkey(f.x);
-      key[i + 1] = fkey(f.y);
-      key[i + 2] = fkey(f.z);
-      key[i + 3] = fkey(f.w);
+      const uint4 f = __ldg(reinterpret_cast<const uint4*>(v + p + i));
+      bits[i] = f.x;
+      bits[i + 1] = f.y;
+      bits[i + 2] = f.z;
+      bits[i + 3] = f.w;
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) key[i] = (p + i < valid) ? fkey(__ldg(v + p + i)) : 0u;
+    for (int i = 0; i < ITEMS; ++i) bits[i] = (p + i < valid) ? __float_as_uint(__ldg(v + p + i)) : 0xFFFFFFFFu;
   }
 }
 
@@ -916,7 +918,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   //    is at most SPAN long).
   const int stride = max(ITEMS, (valid / THREADS) & ~(ITEMS - 1));
   uint32_t key[ITEMS];
-  load_keys<ITEMS>(v, tid * stride, valid, key);
+  load_bits<ITEMS>(v, tid * stride, valid, key);
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) key[i] = fkey(__uint_as_float(key[i]));
   // Sampled positions (s_n) and keys (present: a negative NaN with all bits set reads as key 0 and is
   // left out of the sample; the filter pass below still finds it like any other key).
   int s_n = 0, present = 0;
@@ -948,16 +952,33 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (tid == 0) cand_n[r] = kRowFallback;
     return;
   }
-  // 3. Ordered compaction of every key >= T, SPAN positions per round.
+  // 3. Ordered compaction of every key >= T, SPAN positions per round, on the raw bits: for a threshold
+  //    at or above +0 (every indexer row), key >= T is one signed compare of the bits with T's
+  //    magnitude bits (negative values, negative NaN and the all-ones padding compare below, positive
+  //    NaN above, as in key order); otherwise the keys are formed.
   int32_t* ci = cand_idx + r * cap;
   float* cv = cand_val + r * cap;
+  const bool nonneg = T >= 0x80000000u;
+  const int32_t tbits = static_cast<int32_t>(T & 0x7FFFFFFFu);
   int running = 0;
+  uint32_t next[ITEMS];  // the following round's bits, requested before this round's scan
+  load_bits<ITEMS>(v, tid * ITEMS, valid, next);
   for (int base = 0; base < valid; base += SPAN) {
     const int p = base + tid * ITEMS;
-    load_keys<ITEMS>(v, p, valid, key);
-    uint32_t mask = 0;
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) mask |= (key[i] >= T && key[i] != 0u) ? (1u << i) : 0u;
+    for (int i = 0; i < ITEMS; ++i) key[i] = next[i];  // raw bits from here on
+    if (base + SPAN < valid) load_bits<ITEMS>(v, p + SPAN, valid, next);
+    uint32_t mask = 0;
+    if (nonneg) {
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) mask |= (static_cast<int32_t>(key[i]) >= tbits) ? (1u << i) : 0u;
+    } else {
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t kk = fkey(__uint_as_float(key[i]));
+        mask |= (kk >= T && kk != 0u) ? (1u << i) : 0u;
+      }
+    }
     const int cnt = __popc(mask);
     const int off = excl_scan_once<THREADS>(cnt, sh.scan);
     if (tid == THREADS - 1) sh.total = off + cnt;
@@ -967,7 +988,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (mask & (1u << i)) {
         if (o < cap) {
           ci[o] = cin ? cin[p + i] : static_cast<int32_t>(p + i + idx_offset);
-          cv[o] = fkey_inv(key[i]);
+          cv[o] = __uint_as_float(key[i]);
         }
         ++o;
       }

@@ -370,9 +370,9 @@ class ActQuantWorkload(Workload):
 
 def topk_launches(rows, n, k, reg_max=8192, temp_bytes=256 << 20, num_sms=148):
     """Kernel launches of one library top-k call (mirrors topk_impl in csrc/dsv32.cu with the
-    workspace dsv32_topk_workspace_bytes asks for): one register pass for rows up to 8192; for rows
-    longer than 16384 with at least num_sms rows, the filter (3 launches per row batch); else the
-    staged plan (segment stages + final merge) per row batch."""
+    workspace dsv32_topk_workspace_bytes asks for): one register pass for rows up to 8192; for longer
+    rows with at least num_sms rows, the filter (3 launches per row batch); else the staged plan
+    (segment stages + final merge) per row batch."""
     if n <= reg_max:
         return 1
     plan = [n]
@@ -380,7 +380,7 @@ def topk_launches(rows, n, k, reg_max=8192, temp_bytes=256 << 20, num_sms=148):
         nseg = -(-plan[-1] // reg_max)
         plan.append(nseg * k)
     staged = 2 * plan[1] * 8
-    filt = ((3 * k + 15) // 16 * 16) * 8 + 16 if (n > 2 * reg_max and 3 * k <= reg_max) else 0
+    filt = ((3 * k + 15) // 16 * 16) * 8 + 16 if (n > reg_max and 3 * k <= reg_max) else 0
     per_row = max(staged, filt)
     ws = max(1, min(rows, temp_bytes // per_row)) * per_row
     if filt and rows >= num_sms:

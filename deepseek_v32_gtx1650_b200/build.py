@@ -51,7 +51,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     """Compile csrc/dsv32.cu into LIB_PATH (skipped when up to date). Returns the path."""
     if not force and not needs_build():
         return LIB_PATH
-    tmp = LIB_PATH + ".tmp"
+    tmp = f"{LIB_PATH}.tmp{os.getpid()}"  # per process: ranks that build at once do not clobber each other
     cmd = [_nvcc(), *NVCC_FLAGS, os.path.join(CSRC, "dsv32.cu"), "-o", tmp]
     proc = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
     if proc.returncode != 0:

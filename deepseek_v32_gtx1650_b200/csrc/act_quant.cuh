@@ -135,41 +135,9 @@ DSV32_DEV uint32_t aq_pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Largest magnitude of the 16-bit values packed two per word (bf16x2 / f16x2), two values per
-// instruction: max with .xorsign.abs keeps the larger magnitude of each half (its sign is the xor of
-// the inputs' and is dropped at the end), .NaN propagates a NaN. Exact: a maximum selects an input.
-template <typename T>
-DSV32_DEV uint32_t absmax2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  if constexpr (std::is_same<T, __nv_bfloat16>::value)
-    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  else
-    asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-// |x|max of a lane's values of 16-bit type T held as NW packed words, as fp32 (NaN if any is NaN).
-template <typename T, int NW>
-DSV32_DEV float lane_absmax16(const uint32_t* w) {
-  uint32_t m = w[0];
-#pragma unroll
-  for (int i = 1; i < NW; ++i) m = absmax2<T>(m, w[i]);
-  float lo, hi;
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    lo = __uint_as_float(m << 16);
-    hi = __uint_as_float(m & 0xFFFF0000u);
-  } else {
-    const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&m));
-    lo = p.x;
-    hi = p.y;
-  }
-  return max_nan(fabsf(lo), fabsf(hi));
-}
-
 // EPL values of a group per lane (LPG = 128 / EPL lanes per group, 32 / LPG groups per warp slot),
 // read as EPL * sizeof(T) / 16 consecutive 16-byte vectors; UNROLL group slots per iteration.
-// kPackedAmax (16-bit input): the lane's amax on the packed words (absmax2) instead of per value.
-template <typename T, int EPL, int UNROLL, bool kPackedAmax = false, bool kPrefetch = false>
+template <typename T, int EPL, int UNROLL>
 __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
                                                         float* __restrict__ s, int64_t num_groups,
                                                         int round_scale) {
@@ -187,32 +155,17 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
   pdl_wait();
   pdl_launch_dependents();
 
-  // The raw 16-byte vectors of UNROLL slots, loaded before any is used and kept packed in registers
-  // until their group is processed. kPrefetch: the next iteration's vectors are requested before
-  // this iteration's are processed (two sets in registers).
-  auto load = [&](int64_t b, uint4 (&dst)[UNROLL][NV]) {
+  for (int64_t base = warp * UNROLL; base < slots; base += nwarps * UNROLL) {
+    // All loads of the lane are issued before any is used; the raw vectors stay packed in
+    // registers until their group is processed.
+    uint4 raw[UNROLL][NV];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
-      const int64_t g = (b + u) * GPW + sub;
-      const bool valid = (b + u) < slots && g < num_groups;
+      const int64_t g = (base + u) * GPW + sub;
+      const bool valid = (base + u) < slots && g < num_groups;
       const uint4* src = reinterpret_cast<const uint4*>(x + g * 128 + sl * EPL);
 #pragma unroll
-      for (int j = 0; j < NV; ++j) dst[u][j] = valid ? __ldcs(src + j) : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  const int64_t stride = nwarps * UNROLL;
-  uint4 next[UNROLL][NV];
-  if constexpr (kPrefetch) load(warp * UNROLL, next);
-  for (int64_t base = warp * UNROLL; base < slots; base += stride) {
-    uint4 raw[UNROLL][NV];
-    if constexpr (kPrefetch) {
-#pragma unroll
-      for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-        for (int j = 0; j < NV; ++j) raw[u][j] = next[u][j];
-      if (base + stride < slots) load(base + stride, next);
-    } else {
-      load(base, raw);
+      for (int j = 0; j < NV; ++j) raw[u][j] = valid ? __ldcs(src + j) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
@@ -230,12 +183,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
         }
       }
       float a = 0.f;
-      if constexpr (kPackedAmax && sizeof(T) == 2) {
-        a = lane_absmax16<T, 4 * NV>(reinterpret_cast<const uint32_t*>(raw[u]));
-      } else {
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) a = max_nan(a, fabsf(f[e]));
-      }
+      for (int e = 0; e < EPL; ++e) a = max_nan(a, fabsf(f[e]));
 #pragma unroll
       for (int o = LPG / 2; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
       const float amax = max_nan(a, 1e-4f);  // NaN anywhere in the group -> NaN

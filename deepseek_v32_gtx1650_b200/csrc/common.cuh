@@ -8,7 +8,6 @@
 #pragma once
 
 #include <cstdint>
-#include <type_traits>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>

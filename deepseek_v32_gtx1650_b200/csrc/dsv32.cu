@@ -430,10 +430,10 @@ int topk_reg_launch(const float* vals, int64_t rows, int n, int64_t ld, const in
 constexpr int kTopkRegMax = 512 * 16;                       // longest row a register pass holds
 constexpr int64_t kTopkPreferredBytes = int64_t(256) << 20;  // workspace the library asks for, at most
 
-// Long-row filter (topk_filter_kernel): plain rows longer than two register passes, k small enough
+// Long-row filter (topk_filter_kernel): plain rows longer than one register pass, k small enough
 // that a list of 3 k candidates fits one register pass, and at least as many rows as SMs (with fewer
 // rows the staged plan, which spreads each row's segments over several CTAs, is faster).
-constexpr int kTopkFilterMinN = 2 * kTopkRegMax;
+constexpr int kTopkFilterMinN = kTopkRegMax;
 bool filter_shape(int64_t n, int64_t k) { return n > kTopkFilterMinN && 3 * k <= kTopkRegMax; }
 int filter_cap(int k) { return (3 * k + 15) / 16 * 16; }
 int64_t filter_per_row(int k) { return int64_t(filter_cap(k)) * 8 + 16; }

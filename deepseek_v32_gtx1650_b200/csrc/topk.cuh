@@ -915,8 +915,11 @@ __global__ void __launch_bounds__(THREADS, 2)
     return;
   }
   // 1. Sample: thread t reads ITEMS consecutive positions at t * stride (the whole visible row when it
-  //    is at most SPAN long).
-  const int stride = max(ITEMS, (valid / THREADS) & ~(ITEMS - 1));
+  //    is at most SPAN long). The stride is rounded to a 16-byte multiple only when that keeps at least
+  //    half of it, so short rows are sampled over their whole length.
+  int stride = valid / THREADS;
+  if (stride >= 2 * ITEMS) stride &= ~(ITEMS - 1);
+  stride = max(stride, ITEMS);
   uint32_t key[ITEMS];
   load_bits<ITEMS>(v, tid * stride, valid, key);
 #pragma unroll

@@ -246,9 +246,10 @@ def test_steady_state_calls_allocate_no_device_memory():
 
 
 @pytest.mark.parametrize("n,k,ties", [(20000, 2048, False), (40000, 2048, True), (65536, 1000, False),
-                                      (131072, 2048, True), (17000, 2730, False)])
+                                      (131072, 2048, True), (17000, 2730, False), (12000, 2048, False),
+                                      (16384, 2048, True), (8200, 100, False)])
 def test_long_rows_filter_equals_oracle(n, k, ties):
-    """Rows longer than two register passes, at least one per SM (160 rows): each row is reduced to the
+    """Rows longer than one register pass, at least one per SM (160 rows): each row is reduced to the
     keys at or above a sampled threshold, in position order, then selected in one register pass. The
     selection equals the oracle's deterministic top-k, values and ties included."""
     rows = 160

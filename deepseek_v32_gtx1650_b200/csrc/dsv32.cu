@@ -99,12 +99,18 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<32, true, 2>, gemm::SwapSmem<32, 2>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, false, 2>, gemm::SwapSmem<64, 2>::kAlloc));
       DSV32_CUDA_TRY(set_smem(gemm::int8_gemm_swap_kernel<64, true, 2>, gemm::SwapSmem<64, 2>::kAlloc));
-      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128>, index::Cfg<64, 128>::kAlloc));
-      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128>, index::Cfg<32, 128>::kAlloc));
-      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128>, index::Cfg<16, 128>::kAlloc));
-      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 64>, index::Cfg<64, 64>::kAlloc));
-      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 64>, index::Cfg<32, 64>::kAlloc));
-      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64>, index::Cfg<16, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128, false>, index::Cfg<64, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 128, true>, index::Cfg<64, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128, false>, index::Cfg<32, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 128, true>, index::Cfg<32, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128, false>, index::Cfg<16, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 128, true>, index::Cfg<16, 128>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 64, false>, index::Cfg<64, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<64, 64, true>, index::Cfg<64, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 64, false>, index::Cfg<32, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<32, 64, true>, index::Cfg<32, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64, false>, index::Cfg<16, 64>::kAlloc));
+      DSV32_CUDA_TRY(set_smem(index::int8_index_kernel<16, 64, true>, index::Cfg<16, 64>::kAlloc));
       {
         int nb = 0;
         DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
@@ -340,10 +346,20 @@ int gemm_impl(const int8_t* a, const float* a_s, const int8_t* b, const float* b
   return gemm_launch(plan, a, a_s, b, b_s, c, c_dtype, m, n, k, partials, ws, stream);
 }
 
+// Selection outputs the indexer writes itself: query rows m < m_triv (each sees at most k keys, so its
+// top-k is its first k positions) get idx / val [row * k + j] = (j + key_offset, score or -inf).
+struct IndexSel {
+  int32_t* idx = nullptr;
+  float* val = nullptr;
+  int k = 0;
+  int m_triv = 0;
+  int key_offset = 0;
+};
+
 template <int H, int D>
 int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w, const float* k_s, float* out,
                  int64_t batch, int64_t m, int64_t n, int causal, int64_t start, int64_t k_ld, int fill_masked,
-                 int num_sms, cudaStream_t st) {
+                 const IndexSel& sel, int num_sms, cudaStream_t st) {
   using namespace dsv32::index;
   using C = Cfg<H, D>;
   const int64_t nqb = (m + C::QB - 1) / C::QB;
@@ -358,17 +374,19 @@ int index_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK, const float* w,
   const int64_t units = batch * nqb * chunks;
   if (units > 0x7FFFFFFFLL) return DSV32_ERR_UNSUPPORTED;
   const int64_t grid = units < num_sms ? units : num_sms;  // persistent: one CTA per SM
-  return launch(int8_index_kernel<H, D>, static_cast<unsigned>(grid), kThreads, C::kAlloc, st,
+  auto* kernel = sel.m_triv > 0 ? int8_index_kernel<H, D, true> : int8_index_kernel<H, D, false>;
+  return launch(kernel, static_cast<unsigned>(grid), kThreads, C::kAlloc, st,
                 "int8_index_kernel launch", tmQ, tmK, w, k_s, out, static_cast<int>(m), static_cast<int>(n), causal,
                 static_cast<long long>(start), static_cast<int>(tpc), static_cast<int>(chunks),
-                static_cast<int>(units), static_cast<long long>(k_ld), fill_masked);
+                static_cast<int>(units), static_cast<long long>(k_ld), fill_masked, sel.idx, sel.val, sel.k,
+                sel.m_triv, sel.key_offset);
 }
 
 // k_ld: keys between the starts of consecutive batches of k and k_s (0: n, the contiguous layout).
 // fill_masked == 0: key tiles no query of a block can see are left unwritten in `out`.
 int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* out, int64_t batch,
                int64_t m, int64_t n, int64_t heads, int64_t dim, int causal, int64_t start, int64_t k_ld,
-               int fill_masked, void* stream) {
+               int fill_masked, void* stream, const IndexSel& sel = IndexSel{}) {
   if (!q || !w || !k || !k_s || !out) return DSV32_ERR_INVALID_ARG;
   if (batch < 1 || m < 1 || n < 1) return DSV32_ERR_INVALID_ARG;
   if (k_ld == 0) k_ld = n;
@@ -394,7 +412,7 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
   const int S = info->num_sms;
 #define DSV32_INDEX_CASE(HH, DD)                                                                              \
   if (heads == HH && dim == DD)                                                                               \
-    return index_launch<HH, DD>(tmQ, tmK, w, k_s, out, batch, m, n, causal, start, k_ld, fill_masked, S, st);
+    return index_launch<HH, DD>(tmQ, tmK, w, k_s, out, batch, m, n, causal, start, k_ld, fill_masked, sel, S, st);
   DSV32_INDEX_CASE(64, 128)
   DSV32_INDEX_CASE(32, 128)
   DSV32_INDEX_CASE(16, 128)
@@ -789,11 +807,20 @@ int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, cons
   if (workspace && (!aligned16(workspace) || workspace_bytes < 0)) return DSV32_ERR_INVALID_ARG;
   // Without scores_out the masked tiles of causal rows stay unwritten: the selection never reads a
   // causal row past its visible length.
+  // Causal single-batch calls: the leading rows that see at most topk keys (start + m + 1 <= topk) take
+  // their first topk positions, which the indexer writes itself; the selection runs on the rest.
+  IndexSel sel;
+  if (causal && batch == 1 && m * topk <= 0x7FFFFFFFLL && key_offset >= 0 && key_offset + n <= 0x7FFFFFFFLL) {
+    const int64_t mt = n <= topk ? m : std::min<int64_t>(m, std::max<int64_t>(0, topk - start));
+    sel = IndexSel{out_idx, out_val, static_cast<int>(topk), static_cast<int>(mt), static_cast<int>(key_offset)};
+  }
   if (int st = index_impl(q, w, k, k_s, scores, batch, m, n, heads, dim, causal, start, k_ld,
-                          (scores_out || !causal) ? 1 : 0, stream))
+                          (scores_out || !causal) ? 1 : 0, stream, sel))
     return st;
-  return topk_impl(scores, batch * m, n, n, nullptr, 0, key_offset, topk, out_idx, out_val, workspace,
-                   workspace_bytes, stream, causal ? m : 0, start);
+  const int64_t mt = sel.m_triv;
+  if (mt == m) return DSV32_OK;
+  return topk_impl(scores + mt * n, batch * m - mt, n, n, nullptr, 0, key_offset, topk, out_idx + mt * topk,
+                   out_val + mt * topk, workspace, workspace_bytes, stream, causal ? m - mt : 0, start + mt);
 }
 
 int dsv32_rotate_quant(const void* x, int x_dtype, int64_t rows, int rotate, int8_t* y, float* s,

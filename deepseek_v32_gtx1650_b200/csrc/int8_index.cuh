@@ -24,6 +24,10 @@
 //               neither loaded nor multiplied (the reference's tile skip, kernels.py:145-148). With
 //               fill_masked == 0 (scores used only as the selection's scratch, whose causal rows are
 //               never read past their visible length) those tiles are left unwritten.
+// Selected rows (kSel; the fused indexer + top-k of one causal batch): rows m < m_triv see at most
+// sel_k keys, so their top-sel_k is their first sel_k positions in order. The epilogue writes their
+// visible scores and ids straight to the selection outputs and the -inf writer their masked ones;
+// their score rows are written only with fill_masked (scores kept as output).
 // Keys and their scales of batch b start at key b * ks_ld (ks_ld >= N: a cache with spare capacity
 // is read in place).
 //
@@ -116,12 +120,15 @@ DSV32_DEV int unit_of_round(int r, int units) {
   return idx < units ? static_cast<int>(idx) : -1;
 }
 
-template <int H, int D>
+// kSel: the launch selects the leading rows itself (m_triv > 0); kept out of the plain instantiation,
+// whose epilogue loop it would otherwise lengthen.
+template <int H, int D, bool kSel>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_index_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const float* __restrict__ w, const float* __restrict__ k_s, float* __restrict__ out, int M,
                       int N, int causal, long long start, int tiles_per_chunk, int num_chunks, int units,
-                      long long ks_ld, int fill_masked) {
+                      long long ks_ld, int fill_masked, int32_t* __restrict__ sel_idx,
+                      float* __restrict__ sel_val, int sel_k, int m_triv, int key_offset) {
   using C = Cfg<H, D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -256,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ -inf for invisible key tiles
     const int ft = lane;
     const bool vec4 = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
-    for (int r = 0; fill_masked; ++r) {
+    for (int r = 0; fill_masked || kSel; ++r) {
       const int idx = unit_of_round(r, units);
       if (idx < 0) break;
       const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
@@ -267,14 +274,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q = 0; q < C::QB; ++q) {
         const int m = un.m0 + q;
         if (m >= M) break;
-        float* row = out_b + static_cast<int64_t>(m) * N;
-        if (vec4) {  // n_lo is a multiple of 128 and rows are 16-byte aligned
-          float4* row4 = reinterpret_cast<float4*>(row);
-          const float4 ninf4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          for (int n4 = n_lo / 4 + ft; n4 < n_hi / 4; n4 += 32) row4[n4] = ninf4;
-          for (int n = (n_hi & ~3) + ft; n < n_hi; n += 32) row[n] = -INFINITY;
-        } else {
-          for (int n = n_lo + ft; n < n_hi; n += 32) row[n] = -INFINITY;
+        if (fill_masked) {
+          float* row = out_b + static_cast<int64_t>(m) * N;
+          if (vec4) {  // n_lo is a multiple of 128 and rows are 16-byte aligned
+            float4* row4 = reinterpret_cast<float4*>(row);
+            const float4 ninf4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            for (int n4 = n_lo / 4 + ft; n4 < n_hi / 4; n4 += 32) row4[n4] = ninf4;
+            for (int n = (n_hi & ~3) + ft; n < n_hi; n += 32) row[n] = -INFINITY;
+          } else {
+            for (int n = n_lo + ft; n < n_hi; n += 32) row[n] = -INFINITY;
+          }
+        }
+        if (kSel && m < m_triv) {  // a row selected here: its masked positions below sel_k
+          const int64_t so = (static_cast<int64_t>(un.b) * M + m) * sel_k;
+          for (int n = n_lo + ft; n < min(n_hi, sel_k); n += 32) {
+            sel_val[so + n] = -INFINITY;
+            sel_idx[so + n] = n + key_offset;
+          }
         }
       }
     }
@@ -312,10 +328,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* ksp = k_s + static_cast<int64_t>(un.b) * ks_ld + n_base;
       float* outp[C::kQPerWarp];
       int lim[C::kQPerWarp];  // the key of tile offset t is visible to query q iff t <= lim[q]
+      // Rows selected here (m < m_triv: at most sel_k visible keys) have their scores written only
+      // when kept as output. sel_unit (warp-uniform): some query of this warp is such a row.
+      const bool sel_unit = kSel && un.m0 + q_first < m_triv;
 #pragma unroll
       for (int q = 0; q < C::kQPerWarp; ++q) {
         const int m = un.m0 + q_first + q;
-        outp[q] = (m < M) ? out + (static_cast<int64_t>(un.b) * M + m) * N + n_base : nullptr;
+        outp[q] = (m < M && (fill_masked || !kSel || m >= m_triv))
+                      ? out + (static_cast<int64_t>(un.b) * M + m) * N + n_base
+                      : nullptr;
         const long long l = causal ? start + m - n_base : 0x7FFFFFFFLL;
         lim[q] = static_cast<int>(l < -1 ? -1 : (l > 0x7FFFFFFFLL ? 0x7FFFFFFFLL : l));
       }
@@ -357,13 +378,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[q][1] = __ffma2_rn(v1, make_float2(w4.z, w4.w), acc[q][1]);
           }
         }
-        if (n_ok) {
+        if (n_ok && !sel_unit) {
 #pragma unroll
           for (int q = 0; q < C::kQPerWarp; ++q) {
             if (outp[q]) {
               float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
               if (toff > lim[q]) sc = -INFINITY;
               outp[q][toff] = sc;
+            }
+          }
+        } else if (kSel && n_ok) {
+#pragma unroll
+          for (int q = 0; q < C::kQPerWarp; ++q) {
+            float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
+            if (toff > lim[q]) sc = -INFINITY;
+            if (outp[q]) outp[q][toff] = sc;
+            const int m = un.m0 + q_first + q;
+            if (m < m_triv && toff + n_base < sel_k) {  // output j of such a row is position j
+              const int64_t so = (static_cast<int64_t>(un.b) * M + m) * sel_k + toff + n_base;
+              sel_val[so] = sc;
+              sel_idx[so] = toff + n_base + key_offset;
             }
           }
         }

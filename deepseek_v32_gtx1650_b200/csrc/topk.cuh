@@ -8,9 +8,12 @@
 // so "lower position" is "lower global key index", and the merge of per-shard top-k lists
 // reproduces the single-GPU selection exactly.
 //
-// NaN: keys follow the bit pattern, so a NaN with the sign bit clear (every NaN the indexer or any
-// fp32 arithmetic produces) ranks above +inf, as in torch.topk; a NaN with the sign bit set, which
-// only a caller's own scores can hold, ranks below -inf (torch.topk ranks every NaN first).
+// NaN: every NaN, of either sign, ranks above +inf and NaNs tie with one another (torch.topk's
+// order: its radix keys send each NaN to the all-ones key). A NaN selected by the register kernel
+// comes back as the canonical NaN (0x7FFFFFFF, the value of its key; rewriting it with its own bits
+// costs registers the kernel does not have), elsewhere with its own bits. -0.0 ranks just below
+// +0.0 (distinct keys, as in torch.topk on the GPU). So no key ranks below -inf, and the masked
+// (-inf) tail of a row is the bottom of its order.
 //
 // Algorithm (radix select on order-preserving uint32 keys; larger float -> larger key):
 //  1. Block reductions give the number of finite values and the min / max finite key. Masked
@@ -34,11 +37,16 @@ namespace dsv32 {
 namespace topk {
 
 constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // key of -inf: below every finite value
+constexpr uint32_t kNaNKey = 0xFFFFFFFFu;     // key of every NaN: above +inf (0xFF800000)
 constexpr int kHistBits = 11;
 
+// Order-preserving key: negative floats have all bits flipped, the others the sign bit raised. NaN is
+// tested first: written as an OR with the sign mask, the non-NaN mapping may be compiled to a
+// floating-point negate of the absolute value, which turns a NaN into the canonical NaN.
 DSV32_DEV uint32_t fkey(float f) {
   const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  const uint32_t k = u ^ (static_cast<uint32_t>(static_cast<int32_t>(u) >> 31) | 0x80000000u);
+  return f != f ? kNaNKey : k;
 }
 
 DSV32_DEV float fkey_inv(uint32_t k) {
@@ -47,8 +55,8 @@ DSV32_DEV float fkey_inv(uint32_t k) {
   return __uint_as_float(k ^ flip);
 }
 
-// Keys of a row fall into: "above" (> the -inf key: finite, +inf, +NaN), the -inf key, and
-// below it (negative NaN). Masked -inf entries are counted, never histogrammed.
+// Keys of a row fall into: "above" (> the -inf key: finite, +inf, NaN) and the -inf key. Masked
+// -inf entries are counted, never histogrammed.
 DSV32_DEV bool prefix_match(uint32_t key, uint32_t prefix, int shift) {
   return shift >= 32 || (key >> shift) == (prefix >> shift);
 }
@@ -226,9 +234,8 @@ struct RowParts {
   int len, n;
 };
 
-// Positions past n hold key 0 (below every real key except the all-ones negative NaN): they never
-// count as above -inf, never reach a histogram while the floor is above -inf, and never equal a
-// threshold >= the -inf key. Only the negative-NaN path (threshold below -inf) checks positions.
+// Positions past n hold key 0 (below every real key): they never count as above -inf, never reach a
+// histogram, and never equal a threshold, which is at least the -inf key.
 // Causal rows: input row r is causal row r + causal_row0 (a batch of a larger problem).
 // Segmented form: output row r' = blockIdx.x selects from segment r' % nseg (positions
 // [seg0, seg0 + seg_len) of input row r' / nseg); nseg = 1, seg_len = n_total is the plain top-k.
@@ -254,7 +261,10 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int wid = tid >> 5;
-  const long long out_row = blockIdx.x;
+  // Causal rows are dealt out longest first (their visible length grows with the row), so the short
+  // rows' copies fill the end of the launch instead of delaying the long selections.
+  const long long out_row = (causal_m > 0 && nseg == 1) ? static_cast<long long>(gridDim.x) - 1 - blockIdx.x
+                                                        : static_cast<long long>(blockIdx.x);
   const long long row = out_row / nseg;
   const int seg0 = static_cast<int>(out_row % nseg) * seg_len;
   const int n = min(seg_len, n_total - seg0);
@@ -290,6 +300,29 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   }
   pdl_wait();
   pdl_launch_dependents();
+  // 0. A row with at most k visible positions (a causal row that sees <= k keys) selects exactly its
+  //    first k positions: no key ranks below the masked -inf tail, and the tail's ties go to the
+  //    lowest positions. Output j is position j, copied straight to the outputs.
+  if (valid <= k) {
+    int32_t* oi = out_idx + out_row * k;
+    float* ov = out_val + out_row * k;
+    if (parts.n > 0) {
+      for (int j = tid; j < k; j += THREADS) {
+        const int pj = (seg0 + j) / parts.len;
+        const long long off = row * parts.ld + (seg0 + j - pj * parts.len);
+        oi[j] = parts.id[pj][off];
+        ov[j] = j < valid ? __ldg(parts.v[pj] + off) : -INFINITY;
+      }
+    } else {
+      const float* v = vals + row * ld + seg0;
+      const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
+      for (int j = tid; j < k; j += THREADS) {
+        oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
+        ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
+      }
+    }
+    return;
+  }
   for (int i = tid; i < kRegBins; i += THREADS) sh.u.hist[i] = 0;  // first radix pass
   uint32_t key[ITEMS];
   // Each thread owns ITEMS consecutive positions (position order = thread order). Positions in
@@ -308,39 +341,9 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
     for (int i = 0; i < ITEMS; ++i)
       key[i] = (pos0 + i < valid) ? fkey(__ldg(tv + i)) : (pos0 + i < n ? kNegInfKey : 0u);
   }
-  // 0. A row with at most k visible positions (a causal row that sees <= k keys) selects exactly its
-  //    first k positions: every visible value is above the masked -inf tail, and the tail's ties go
-  //    to the lowest positions. The only exception is a visible negative NaN (below -inf), which
-  //    sends the row down the general path.
-  if (valid <= k) {
-    bool neg_nan = false;
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) neg_nan |= (pos0 + i < valid) && key[i] < kNegInfKey;
-    if (!__syncthreads_or(neg_nan)) {  // (the barrier also orders the histogram clear above)
-      // Output j is position j: a coalesced copy (the visible scores are re-read from L1 / L2).
-      int32_t* oi = out_idx + out_row * k;
-      float* ov = out_val + out_row * k;
-      if (parts.n > 0) {
-        for (int j = tid; j < k; j += THREADS) {
-          const int pj = (seg0 + j) / parts.len;
-          const long long off = row * parts.ld + (seg0 + j - pj * parts.len);
-          oi[j] = parts.id[pj][off];
-          ov[j] = j < valid ? __ldg(parts.v[pj] + off) : -INFINITY;
-        }
-      } else {
-        const float* v = vals + row * ld + seg0;
-        const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
-        for (int j = tid; j < k; j += THREADS) {
-          oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
-          ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
-        }
-      }
-      return;
-    }
-  }
-  // 1. Common case, at least k values above -inf (every indexer row past the fast path): statistics of
-  //    the keys above -inf behind one barrier (which also orders the histogram clear before pass 1),
-  //    with keys at or below -inf mapped to the top of the unsigned range for the minimum.
+  // 1. Statistics of the keys above -inf behind one barrier (which also orders the histogram clear
+  //    before pass 1), with the -inf and padding keys mapped to the top of the unsigned range for the
+  //    minimum.
   {
     int na = 0;
     uint32_t mnw = 0xFFFFFFFFu, mx = 0u;
@@ -360,6 +363,11 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
     }
   }
   __syncthreads();
+  // The threshold key T and krem, how many of the keys equal to T are taken (lowest positions first).
+  // With fewer than k keys above -inf: all of them, then the lowest-position -inf entries (no key
+  // ranks below -inf; padding keys 0 never reach T).
+  uint32_t T = kNegInfKey;
+  int krem;
   {
     int above = 0;
     uint32_t mnw = 0xFFFFFFFFu, mx = 0u;
@@ -369,6 +377,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
       mnw = min(mnw, sh.red[2][w]);
       mx = max(mx, sh.red[3][w]);
     }
+    krem = k - above;
     if (above >= k) {
       // 2. Radix select among the keys above -inf. Past the first pass the open bin is at most 2^21
       //    keys wide and never straddles the -inf key (a multiple of 2^23 plus 2^23 - 1), so a prefix
@@ -376,8 +385,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
       const uint32_t mn = mnw + (kNegInfKey + 1u);
       int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);
       uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
-      int krem = k;
-      uint32_t T = 0u;
+      krem = k;
       bool first = true, resolved = false;
       while (shift > 0) {
         const int d = min(kRegBits, shift);
@@ -460,246 +468,49 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
         }
       }
       if (!resolved) T = prefix;
-      // 3. Ordered compaction; T is above -inf, so masked and padding keys are never selected.
-      uint32_t gmask = 0, emask = 0;
-#pragma unroll
-      for (int i = 0; i < ITEMS; ++i) {
-        gmask |= key[i] > T ? (1u << i) : 0u;
-        emask |= key[i] == T ? (1u << i) : 0u;
-      }
-      const int eq = __popc(emask);
-      const int packed = excl_scan_once<THREADS>((__popc(gmask) << 16) | eq, sh.scan);  // n <= 65535
-      const int eq_before = packed & 0xFFFF;
-      const int take = max(0, min(eq, krem - eq_before));
-      while (__popc(emask) > take) emask &= ~(0x80000000u >> __clz(emask));  // drop the highest
-      const uint32_t smask = gmask | emask;
-      const int o = (packed >> 16) + min(eq_before, krem);
-      int32_t* oi = out_idx + out_row * k;
-      float* ov = out_val + out_row * k;
-      const bool staged = k <= kStageMax;
-      int32_t* si = staged ? sh.u.out.idx : oi;
-      float* sv = staged ? sh.u.out.val : ov;
-      if (cand_idx || parts.n > 0) {
-        const int32_t* ti = thread_ids();
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-          if (smask & (1u << i)) {
-            const int slot = o + __popc(smask & ((1u << i) - 1u));
-            si[slot] = ti[i];
-            sv[slot] = fkey_inv(key[i]);
-          }
-        }
-      } else {
-        const int32_t id0 = static_cast<int32_t>(pos0 + seg0 + idx_offset);  // ids are int32
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-          const int slot = o + __popc(smask & ((1u << i) - 1u));
-          if (smask & (1u << i)) {
-            si[slot] = id0 + i;
-            sv[slot] = fkey_inv(key[i]);
-          }
-        }
-      }
-      if (staged) {
-        __syncthreads();
-        copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
-      }
-      return;
     }
-  }
-  __syncthreads();  // the general path below rewrites the statistics slots read above
-  // General path (fewer than k values above -inf, so masked -inf or negative NaN keys are selected):
-  // row statistics, counts above / at the -inf key and the key range of the values above -inf.
-  {
-    int na = 0, ni = 0;
-    uint32_t mn = 0xFFFFFFFFu, mx = 0u;
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      const bool a = key[i] > kNegInfKey;
-      na += a ? 1 : 0;
-      ni += key[i] == kNegInfKey ? 1 : 0;
-      mn = a ? min(mn, key[i]) : mn;
-      mx = a ? max(mx, key[i]) : mx;
-    }
-    const uint32_t r0 = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(na));
-    const uint32_t r1 = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(ni));
-    const uint32_t r2 = __reduce_min_sync(0xffffffffu, mn);
-    const uint32_t r3 = __reduce_max_sync(0xffffffffu, mx);
-    if (lane == 0) {
-      sh.red[0][wid] = r0;
-      sh.red[1][wid] = r1;
-      sh.red[2][wid] = r2;
-      sh.red[3][wid] = r3;
-    }
-  }
-  __syncthreads();
-  int above = 0, ninf = 0;
-  uint32_t mn = 0xFFFFFFFFu, mx = 0u;
-#pragma unroll
-  for (int w = 0; w < W; ++w) {
-    above += static_cast<int>(sh.red[0][w]);
-    ninf += static_cast<int>(sh.red[1][w]);
-    mn = min(mn, sh.red[2][w]);
-    mx = max(mx, sh.red[3][w]);
-  }
-  uint32_t T;
-  int krem;
-  if (above < k && above + ninf >= k) {
-    T = kNegInfKey;  // all values above -inf, then the lowest-position -inf entries
-    krem = k - above;
-  } else {
-    // 2. Radix select among the participating keys: those above -inf, or (negative NaNs needed,
-    //    never for indexer scores) every real position.
-    const bool nan_path = above < k;
-    uint32_t floor_key = kNegInfKey + 1u;
-    if (nan_path) {
-      floor_key = 0u;
-      mn = 0xFFFFFFFFu;
-      mx = 0u;
-#pragma unroll
-      for (int i = 0; i < ITEMS; ++i) {
-        if (pos0 + i < n) {
-          mn = min(mn, key[i]);
-          mx = max(mx, key[i]);
-        }
-      }
-      mn = __reduce_min_sync(0xffffffffu, mn);
-      mx = __reduce_max_sync(0xffffffffu, mx);
-      if (lane == 0) {
-        sh.red[2][wid] = mn;
-        sh.red[3][wid] = mx;
-      }
-      __syncthreads();
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        mn = min(mn, sh.red[2][w]);
-        mx = max(mx, sh.red[3][w]);
-      }
-    }
-    int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);  // bits [shift, 32) common to every participant
-    uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
-    krem = k;
-    bool first = true, resolved = false;
-    while (shift > 0) {
-      const int d = min(kRegBits, shift);
-      const int nbins = 1 << d;
-      const int ns = shift - d;
-      if (!first) {
-        for (int i = tid; i < nbins; i += THREADS) sh.u.hist[i] = 0;
-        __syncthreads();
-      }
-#pragma unroll
-      for (int i = 0; i < ITEMS; ++i) {
-        const bool part = nan_path ? (pos0 + i < n) : (key[i] >= floor_key);
-        if (part && (first || prefix_match(key[i], prefix, shift)))
-          atomicAdd(&sh.u.hist[(key[i] >> ns) & (nbins - 1)], 1);
-      }
-      first = false;
-      __syncthreads();
-      // The digit holding the krem-th largest participating key: bins in descending order,
-      // `per` consecutive bins per thread (read as 16-byte vectors: no bank conflicts).
-      const int per = (nbins + THREADS - 1) / THREADS;
-      int local = 0;
-      if ((per & 3) == 0) {
-        const int4* hv = reinterpret_cast<const int4*>(sh.u.hist + (nbins - (tid + 1) * per));
-        for (int j = 0; j < per / 4; ++j) {
-          const int4 h4 = hv[j];
-          local += (h4.x + h4.y) + (h4.z + h4.w);
-        }
-      } else {
-        for (int j = 0; j < per; ++j) {
-          const int bin = nbins - 1 - (tid * per + j);
-          if (bin >= 0) local += sh.u.hist[bin];
-        }
-      }
-      const int before = excl_scan_once<THREADS>(local, sh.scan);
-      if (before < krem && krem <= before + local) {
-        int acc = before;
-        for (int j = 0; j < per; ++j) {
-          const int bin = nbins - 1 - (tid * per + j);
-          const int c = sh.u.hist[bin];
-          if (acc + c >= krem) {
-            sh.prefix = prefix | (uint32_t(bin) << ns);
-            sh.krem = krem - acc;
-            sh.bin_cnt = c;
-            sh.cand_n = 0;
-            break;
-          }
-          acc += c;
-        }
-      }
-      __syncthreads();  // also separates this pass's histogram reads from the next clear
-      prefix = sh.prefix;
-      krem = sh.krem;
-      const int cnt = sh.bin_cnt;
-      shift = ns;
-      if (shift > 0 && cnt <= 32) {
-        // At most a warp's worth of keys share the digits found so far: one warp ranks them
-        // (register shuffles) instead of running more passes.
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-          const bool part = nan_path ? (pos0 + i < n) : (key[i] >= floor_key);
-          if (part && prefix_match(key[i], prefix, shift)) sh.cand[atomicAdd(&sh.cand_n, 1)] = key[i];
-        }
-        __syncthreads();
-        if (wid == 0) {
-          const uint32_t mine = lane < cnt ? sh.cand[lane] : 0u;
-          int g = 0, e = 0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const uint32_t c = __shfl_sync(0xffffffffu, mine, j);
-            g += (j < cnt && c > mine) ? 1 : 0;
-            e += (j < cnt && c == mine) ? 1 : 0;
-          }
-          if (lane < cnt && g < krem && krem <= g + e) {  // every holder of this key writes the same values
-            sh.T = mine;
-            sh.krem = krem - g;
-          }
-        }
-        __syncthreads();
-        T = sh.T;
-        krem = sh.krem;
-        resolved = true;
-        break;
-      }
-    }
-    if (!resolved) T = prefix;
   }
   // 3. Ordered compaction: per-thread bit masks of the keys above / at the threshold, one scan of the
   //    packed counts gives every thread its output slot, and a popcount ranks each selected key.
-  const bool check_pos = T < kNegInfKey;  // only a negative-NaN threshold can equal the padding key
+  //    T is at least the -inf key, so padding keys are never selected.
   uint32_t gmask = 0, emask = 0;
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
-    const bool real = !check_pos || pos0 + i < n;
-    gmask |= (key[i] > T && real) ? (1u << i) : 0u;
-    emask |= (key[i] == T && real) ? (1u << i) : 0u;
+    gmask |= key[i] > T ? (1u << i) : 0u;
+    emask |= key[i] == T ? (1u << i) : 0u;
   }
   const int eq = __popc(emask);
   const int packed = excl_scan_once<THREADS>((__popc(gmask) << 16) | eq, sh.scan);  // n <= 65535
   const int eq_before = packed & 0xFFFF;
   // keys equal to the threshold are taken in position order: this thread keeps its first `take`
-  int take = max(0, min(eq, krem - eq_before));
+  const int take = max(0, min(eq, krem - eq_before));
   while (__popc(emask) > take) emask &= ~(0x80000000u >> __clz(emask));  // drop the highest
   const uint32_t smask = gmask | emask;
   const int o = (packed >> 16) + min(eq_before, krem);
   int32_t* oi = out_idx + out_row * k;
   float* ov = out_val + out_row * k;
   const bool staged = k <= kStageMax;
-  const int32_t* ti = thread_ids();
+  int32_t* si = staged ? sh.u.out.idx : oi;
+  float* sv = staged ? sh.u.out.val : ov;
+  // (one loop per id source: a per-entry choice in a single loop costs about 5% of the kernel)
+  if (cand_idx || parts.n > 0) {
+    const int32_t* ti = thread_ids();
 #pragma unroll
-  for (int i = 0; i < ITEMS; ++i) {
-    if (smask & (1u << i)) {
-      const int pos = pos0 + i;
+    for (int i = 0; i < ITEMS; ++i) {
+      if (smask & (1u << i)) {
+        const int slot = o + __popc(smask & ((1u << i) - 1u));
+        si[slot] = ti[i];
+        sv[slot] = fkey_inv(key[i]);
+      }
+    }
+  } else {
+    const int32_t id0 = static_cast<int32_t>(pos0 + seg0 + idx_offset);  // ids are int32
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
       const int slot = o + __popc(smask & ((1u << i) - 1u));
-      const int32_t id = ti ? ti[i] : static_cast<int32_t>(pos + seg0 + idx_offset);
-      const float x = fkey_inv(key[i]);
-      if (staged) {
-        sh.u.out.idx[slot] = id;
-        sh.u.out.val[slot] = x;
-      } else {
-        oi[slot] = id;
-        ov[slot] = x;
+      if (smask & (1u << i)) {
+        si[slot] = id0 + i;
+        sv[slot] = fkey_inv(key[i]);
       }
     }
   }
@@ -729,21 +540,16 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
   if (row_state && row_state[row] != kRowFallback) return;
   const int valid = row_valid(row + causal_row0, n, causal_m, causal_start);
   auto key_at = [&](int i) { return i < valid ? fkey(__ldg(v + i)) : kNegInfKey; };
-  int n_above = 0, n_ninf = 0;
-  for (int i = threadIdx.x; i < n; i += THREADS) {
-    const uint32_t kk = key_at(i);
-    n_above += kk > kNegInfKey ? 1 : 0;
-    n_ninf += kk == kNegInfKey ? 1 : 0;
-  }
+  int n_above = 0;
+  for (int i = threadIdx.x; i < n; i += THREADS) n_above += key_at(i) > kNegInfKey ? 1 : 0;
   const int above = block_sum<THREADS>(n_above, sh.scratch, parity);
-  const int ninf = block_sum<THREADS>(n_ninf, sh.scratch, parity);
   uint32_t T;
   int k_rem;
-  if (above < k && above + ninf >= k) {
+  if (above < k) {  // every key above -inf, then the lowest-position -inf entries (none ranks lower)
     T = kNegInfKey;
     k_rem = k - above;
   } else {
-    const uint32_t floor_key = (above >= k) ? kNegInfKey + 1u : 0u;
+    const uint32_t floor_key = kNegInfKey + 1u;
     uint32_t mn = 0xFFFFFFFFu, mx = 0u;
     for (int i = threadIdx.x; i < n; i += THREADS) {
       const uint32_t kk = key_at(i);
@@ -814,7 +620,7 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
 // k largest of the list (row_len = its length). Every key >= the row's k-th largest is in the list
 // whenever the list holds at least k keys, so the selection, ties included, equals the one over the
 // whole row. A row whose list would hold fewer than k keys or more than cap (a sample far from the
-// row's distribution, masked or negative-NaN keys among the k largest, at most k visible keys) is
+// row's distribution, masked (-inf) keys among the k largest, at most k visible keys) is
 // marked kRowFallback and selected by topk_gmem_kernel instead. One CTA per row.
 constexpr int kFilterThreads = 512;
 constexpr int kFilterItems = 16;
@@ -871,9 +677,9 @@ DSV32_DEV uint32_t block_kth_key(const uint32_t (&key)[ITEMS], int c, FilterShar
   return prefix;
 }
 
-// Keys of ITEMS consecutive positions p .. p + ITEMS - 1 of a row (0 past `valid`).
-// The raw bits of ITEMS consecutive positions p .. p + ITEMS - 1 of a row; all ones past `valid` (whose
-// key, fkey, is 0: no key).
+// The raw bits of ITEMS consecutive positions p .. p + ITEMS - 1 of a row; the bits of -inf past
+// `valid` (masked positions, never selected by the filter).
+constexpr uint32_t kNegInfBits = 0xFF800000u;
 template <int ITEMS>
 DSV32_DEV void load_bits(const float* v, int p, int valid, uint32_t (&bits)[ITEMS]) {
   if ((reinterpret_cast<uintptr_t>(v + p) & 15u) == 0 && p + ITEMS <= valid) {
@@ -887,7 +693,7 @@ DSV32_DEV void load_bits(const float* v, int p, int valid, uint32_t (&bits)[ITEM
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) bits[i] = (p + i < valid) ? __float_as_uint(__ldg(v + p + i)) : 0xFFFFFFFFu;
+    for (int i = 0; i < ITEMS; ++i) bits[i] = (p + i < valid) ? __float_as_uint(__ldg(v + p + i)) : kNegInfBits;
   }
 }
 
@@ -922,47 +728,39 @@ __global__ void __launch_bounds__(THREADS, 2)
   stride = max(stride, ITEMS);
   uint32_t key[ITEMS];
   load_bits<ITEMS>(v, tid * stride, valid, key);
+  const int q0 = tid * stride;
 #pragma unroll
-  for (int i = 0; i < ITEMS; ++i) key[i] = fkey(__uint_as_float(key[i]));
-  // Sampled positions (s_n) and keys (present: a negative NaN with all bits set reads as key 0 and is
-  // left out of the sample; the filter pass below still finds it like any other key).
-  int s_n = 0, present = 0;
+  for (int i = 0; i < ITEMS; ++i) key[i] = (q0 + i < valid) ? fkey(__uint_as_float(key[i])) : 0u;  // 0: no key
+  // Sampled positions (s_n); every one holds a key (no real key is 0).
+  int s_n = 0;
   {
-    int pos = max(0, min(ITEMS, valid - tid * stride)), have = 0;
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) have += key[i] != 0u ? 1 : 0;
-    const int packed = __reduce_add_sync(0xffffffffu, (pos << 16) | have);  // ITEMS * 32 < 2^16
-    if ((tid & 31) == 0) sh.scan[tid >> 5] = packed;
+    const int pos = max(0, min(ITEMS, valid - q0));
+    const int cnt = __reduce_add_sync(0xffffffffu, pos);
+    if ((tid & 31) == 0) sh.scan[tid >> 5] = cnt;
     __syncthreads();
 #pragma unroll
-    for (int w = 0; w < THREADS / 32; ++w) {
-      s_n += sh.scan[w] >> 16;
-      present += sh.scan[w] & 0xFFFF;
-    }
+    for (int w = 0; w < THREADS / 32; ++w) s_n += sh.scan[w];
     __syncthreads();
   }
   // 2. Threshold: the c-th largest sampled key, c scaled so that about 1.5 k keys of the row reach it
-  //    (exactly the k-th largest when the sample is the whole row).
+  //    (exactly the k-th largest when the sample is the whole row). valid > k >= 1, so s_n >= 1.
   long long c_ll = (s_n >= valid) ? k : (3LL * k * s_n + 2LL * valid - 1) / (2LL * valid);
   if (c_ll < 1) c_ll = 1;
-  if (c_ll > present) c_ll = present;
-  if (present == 0) {
-    if (tid == 0) cand_n[r] = kRowFallback;
-    return;
-  }
+  if (c_ll > s_n) c_ll = s_n;
   const uint32_t T = block_kth_key<THREADS, ITEMS>(key, static_cast<int>(c_ll), sh);
-  if (T <= kNegInfKey) {  // -inf or negative NaN among the candidates: the general selection
+  if (T <= kNegInfKey) {  // -inf among the candidates: the general selection
     if (tid == 0) cand_n[r] = kRowFallback;
     return;
   }
-  // 3. Ordered compaction of every key >= T, SPAN positions per round, on the raw bits: for a threshold
-  //    at or above +0 (every indexer row), key >= T is one signed compare of the bits with T's
-  //    magnitude bits (negative values, negative NaN and the all-ones padding compare below, positive
-  //    NaN above, as in key order); otherwise the keys are formed.
+  // 3. Ordered compaction of every key >= T, SPAN positions per round, on the raw bits: key >= T is
+  //    "not below T" as floats (NaN compares unordered, so it qualifies, as its key is the largest);
+  //    otherwise the keys are formed. Positions past the visible length read as -inf, below T.
   int32_t* ci = cand_idx + r * cap;
   float* cv = cand_val + r * cap;
-  const bool nonneg = T >= 0x80000000u;
-  const int32_t tbits = static_cast<int32_t>(T & 0x7FFFFFFFu);
+  // By value unless T is a NaN (NaNs of every payload qualify) or a signed zero (which the
+  // floating-point compare does not tell apart).
+  const bool by_value = T != kNaNKey && T != 0x80000000u && T != 0x7FFFFFFFu;
+  const float tval = fkey_inv(T);
   int running = 0;
   uint32_t next[ITEMS];  // the following round's bits, requested before this round's scan
   load_bits<ITEMS>(v, tid * ITEMS, valid, next);
@@ -972,15 +770,12 @@ __global__ void __launch_bounds__(THREADS, 2)
     for (int i = 0; i < ITEMS; ++i) key[i] = next[i];  // raw bits from here on
     if (base + SPAN < valid) load_bits<ITEMS>(v, p + SPAN, valid, next);
     uint32_t mask = 0;
-    if (nonneg) {
+    if (by_value) {  // x >= T or x unordered (NaN): one compare per value
 #pragma unroll
-      for (int i = 0; i < ITEMS; ++i) mask |= (static_cast<int32_t>(key[i]) >= tbits) ? (1u << i) : 0u;
+      for (int i = 0; i < ITEMS; ++i) mask |= !(__uint_as_float(key[i]) < tval) ? (1u << i) : 0u;
     } else {
 #pragma unroll
-      for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t kk = fkey(__uint_as_float(key[i]));
-        mask |= (kk >= T && kk != 0u) ? (1u << i) : 0u;
-      }
+      for (int i = 0; i < ITEMS; ++i) mask |= fkey(__uint_as_float(key[i])) >= T ? (1u << i) : 0u;
     }
     const int cnt = __popc(mask);
     const int off = excl_scan_once<THREADS>(cnt, sh.scan);

@@ -117,7 +117,9 @@ int64_t dsv32_topk_workspace_bytes(int64_t rows, int64_t n, int64_t k, int npart
 /* Top-k selection per row: replaces torch.topk(scores, k) on the indexer output
  * (test_kernels.py:125, bench_indexer_e2e.py:72-77).
  * Row r of the input is scores[r * ld + 0 .. n). Selects the k largest values (ties at the k-th
- * value: lowest position first) and writes them in increasing position order:
+ * value: lowest position first) and writes them in increasing position order. Order as torch.topk
+ * on the GPU: every NaN (either sign) above +inf, NaNs equal to one another; -0.0 below +0.0. A
+ * selected NaN is written as a NaN (possibly the canonical 0x7FFFFFFF); other values bit for bit:
  * out_idx [rows, k] int32, out_val [rows, k] fp32. The index written for position p is
  * cand_idx[r * cand_ld + p] when cand_idx is non-NULL (merging candidate lists), else p + idx_offset
  * (a shard's first global key). Requires 1 <= k <= n.
@@ -135,7 +137,9 @@ int dsv32_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, const i
  * global key; 0 for a whole cache). k_ld as in dsv32_int8_index.
  * scores_out != 0: `scores` holds the full scores on return (-inf where masked). scores_out == 0:
  * `scores` is scratch, and with causal != 0 its masked entries are left unwritten (the selection
- * never reads a causal row past its visible length).
+ * never reads a causal row past its visible length). With causal != 0 and batch == 1, the rows
+ * that see at most topk keys (query m with start + m < topk) select their first topk positions;
+ * the indexer writes those rows' outputs itself (and their scores only when scores_out != 0).
  * workspace / workspace_bytes: the selection's scratch, as for dsv32_topk (rows = batch * m).
  * out_idx / out_val [batch, m, topk]. Requires 1 <= topk <= n. */
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,

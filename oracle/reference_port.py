@@ -112,15 +112,32 @@ def int8_index_ref(q: np.ndarray, w: np.ndarray, k: np.ndarray, k_s: np.ndarray,
 
 
 # ---------------------------------------------------------------------------------- top-k
+def order_keys(x: np.ndarray) -> np.ndarray:
+    """fp32 -> uint32 keys in the order torch.topk ranks values on the GPU (its radix keys): negative
+    floats with all bits flipped, the others with the sign bit raised, so -0.0 ranks just below +0.0,
+    and every NaN (either sign) the all-ones key, above +inf, NaNs tying with one another."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    key = np.where(u >> np.uint32(31) == 1, ~u, u | np.uint32(0x80000000)).astype(np.uint32)
+    return np.where(np.isnan(x), np.uint32(0xFFFFFFFF), key).astype(np.uint32)
+
+
 def topk_ref(scores: np.ndarray, k: int):
-    """Deterministic top-k per row: the k largest values, ties at the k-th value by lowest position,
-    listed in increasing position order. Returns (idx int64 [..., k], vals [..., k])."""
+    """Deterministic top-k per row (the selection torch.topk makes in test_kernels.py:121-126, with its
+    ties fixed): the k largest values in order_keys order (fp32 scores; wider types by value, NaN
+    first), ties at the k-th key by lowest position, listed in increasing position order.
+    Returns (idx int64 [..., k], vals [..., k])."""
     s = np.asarray(scores)
     n = s.shape[-1]
     flat = s.reshape(-1, n)
     idx = np.empty((flat.shape[0], k), dtype=np.int64)
+    pos = np.arange(n)
     for r in range(flat.shape[0]):
-        order = np.lexsort((np.arange(n), -flat[r]))  # value desc, then position asc
+        row = flat[r]
+        if row.dtype == np.float32:
+            order = np.lexsort((pos, -order_keys(row).astype(np.int64)))  # key desc, then position asc
+        else:
+            nan = np.isnan(row)
+            order = np.lexsort((pos, -np.where(nan, 0.0, row), ~nan))  # NaN, value desc, position asc
         idx[r] = np.sort(order[:k])
     vals = np.take_along_axis(flat, idx, axis=1)
     return idx.reshape(*s.shape[:-1], k), vals.reshape(*s.shape[:-1], k)

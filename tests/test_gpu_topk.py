@@ -42,6 +42,63 @@ def test_select_topk_with_masked_tail():
     assert O.topk_valid(npy(idx), s.numpy(), 2048)
 
 
+def _assert_same_values(got, ref):
+    """NaN where the reference has NaN (any payload); every other value bit for bit."""
+    got, ref = np.asarray(got, np.float32), np.asarray(ref, np.float32)
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    np.testing.assert_array_equal(got.view(np.int32)[~nan], ref.view(np.int32)[~nan])
+
+
+def _nan_rows(rows, n, seed):
+    """Rows with NaNs of both signs and several payloads, infinities, masked tails and signed zeros."""
+    g = torch.Generator().manual_seed(seed)
+    s = torch.randn(rows, n, generator=g)
+    b = s.view(torch.int32)
+    s[0, 5], s[0, 40] = float("nan"), float("inf")
+    b[0, 17] = -4194304                                  # 0xFFC00000: NaN with the sign bit set
+    s[1] = float("-inf")
+    s[1, 3] = float("nan")
+    b[1, 9] = -1                                         # 0xFFFFFFFF: all bits set
+    s[2, 100:] = float("-inf")
+    b[2, 10] = 0x7F800123                                # NaN with a payload
+    s[3, ::2] = 0.0
+    s[3, 1::4] = -0.0
+    b[4, ::3] = 0x7FC00000
+    b[4, 1::7] = -8388607                                # 0xFF800001: the lowest negative NaN bits
+    return s
+
+
+@pytest.mark.parametrize("n,k,rows", [(300, 64, 6), (1536, 512, 6), (1536, 16, 6), (20000, 2048, 160),
+                                      (40000, 2048, 6), (131072, 2048, 5)])
+def test_select_topk_nan_and_signed_zero_order(n, k, rows):
+    """Values are ranked as torch.topk ranks fp32 on the GPU: every NaN above +inf (NaNs tie, lowest
+    position first), -0.0 just below +0.0. Covers the register pass, the staged plan (few long rows),
+    the long-row filter and its scratch-free fallback. Values other than NaN are returned bit for bit
+    (signed zeros included); a selected NaN comes back as a NaN."""
+    s = _nan_rows(rows, n, seed=n + k)
+    idx, vals = D.select_topk(s.to(DEV), k)
+    pick = list(range(min(rows, 6))) + [rows - 1]
+    ri, rv = O.topk_ref(s.numpy()[pick], k)
+    np.testing.assert_array_equal(npy(idx)[pick], ri)
+    _assert_same_values(npy(vals)[pick], rv)
+    assert_no_device_error()
+
+
+def test_merge_of_shard_lists_with_nan_equals_global():
+    """NaN order holds through the merge of per-shard lists (read in place and concatenated)."""
+    n, k, shards = 16384, 2048, 4
+    s = _nan_rows(6, n, seed=99).to(DEV)
+    step = n // shards
+    parts = [D.select_topk(s[:, r * step:(r + 1) * step].contiguous(), k, idx_offset=r * step) for r in range(shards)]
+    midx, mval = D.select_topk_parts([p[1] for p in parts], [p[0] for p in parts], k)
+    gidx, gval = D.select_topk(s, k)
+    assert torch.equal(midx, gidx) and torch.equal(mval.view(torch.int32), gval.view(torch.int32))
+    ri, rv = O.topk_ref(npy(s), k)
+    np.testing.assert_array_equal(npy(gidx), ri)
+    assert_no_device_error()
+
+
 @pytest.mark.parametrize("shards", [2, 4, 8])
 def test_merge_of_shard_topk_equals_global(shards):
     """Key-range sharding: per-shard top-k with global key offsets, candidate lists
@@ -142,6 +199,29 @@ def test_index_topk_causal_batched_with_offset(start):
         ri, rv = O.topk_ref(sc, topk)
         np.testing.assert_array_equal(npy(idx)[b], ri + 4096)
         np.testing.assert_array_equal(npy(vals)[b], rv)
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("start,N,topk", [(-300, 1536, 512), (0, 4096, 2048), (700, 1536, 512), (100, 640, 640),
+                                          (3000, 4096, 512)])
+def test_index_topk_leading_rows_selected_by_the_indexer(start, N, topk):
+    """In a single-batch causal call the leading rows see at most topk keys, so their selection is their
+    first topk positions; the indexer writes it itself and the top-k launch covers the other rows. The
+    result must equal the plain selection over the returned scores, bit for bit, with the scores kept
+    or not, and with NaN (of either sign) in the weights and key scales."""
+    M = 640
+    q, w, k, ks = workloads.index_inputs(1, M, N, seed=31)
+    ks[0, 7] = float("nan")
+    ks[0, 9] = torch.tensor(float("nan")).neg()
+    w[0, 300, 5] = torch.tensor(float("nan")).neg()
+    qd, wd, kd, ksd = q.to(DEV), w.to(DEV), k.to(DEV), ks.to(DEV)
+    scores, idx, vals = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=start, key_offset=77)
+    pidx, pvals = D.select_topk(scores.view(M, N), topk)
+    assert torch.equal(idx.view(M, topk), pidx + 77)
+    assert torch.equal(vals.view(M, topk).view(torch.int32), pvals.view(torch.int32))
+    idx2, vals2 = D.int8_index_topk(qd, wd, kd, ksd, topk=topk, causal=True, start=start, key_offset=77,
+                                    return_scores=False)
+    assert torch.equal(idx2, idx) and torch.equal(vals2.view(torch.int32), vals.view(torch.int32))
     assert_no_device_error()
 
 
@@ -268,8 +348,8 @@ def test_long_rows_filter_equals_oracle(n, k, ties):
 def test_long_rows_filter_fallbacks():
     """Rows on which the sampled threshold misjudges the row (large values only at positions the sample
     skips, so the candidate list overflows; or only at sampled positions, so it holds fewer than k keys)
-    and rows with masked or negative-NaN keys among the k largest are selected by the scratch-free
-    kernel instead: every row still equals the oracle."""
+    and rows with masked keys among the k largest or more NaNs than the list holds are selected by
+    the scratch-free kernel instead: every row still equals the oracle."""
     rows, n, k = 160, 20000, 2048
     g = torch.Generator().manual_seed(3)
     s = torch.rand(rows, n, generator=g)

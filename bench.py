@@ -393,19 +393,19 @@ class IndexWorkload(Workload):
     higher_is_better = False
     dtype = "int8"
 
-    def __init__(self, kind, rank, world, topk=2048):
+    def __init__(self, kind, rank, world, topk=2048, queries=4096):
         self.kind, self.rank, self.world, self.topk = kind, rank, world, topk
         if kind == "prefill":
             self.B, self.M, self.N, self.causal, self.start = 1, 4096, 4096, True, 0
         elif kind == "decode":
             self.B, self.M, self.N, self.causal, self.start = 1, 4, 32768, False, 0
-        else:  # long, keys sharded by range
-            self.B, self.M, self.N, self.causal, self.start = 1, 4096, 131072, True, 131072 - 4096
+        else:  # long, keys sharded by range (queries: fewer rows for profiler captures)
+            self.B, self.M, self.N, self.causal, self.start = 1, queries, 131072, True, 131072 - queries
         self.scaling = "strong" if kind == "long" else "weak"
         self.name = f"index_{kind}"
         self.metric = {"prefill": "indexer prefill ms @4096^2 causal (scores + top-2048)",
                        "decode": "indexer decode ms (4 x 32768, scores + top-2048)",
-                       "long": "indexer long ms (4096 x 131072 causal, key-sharded, top-2048)"}[kind]
+                       "long": f"indexer long ms ({self.M} x 131072 causal, key-sharded, top-2048)"}[kind]
         self.unit = "ms"
         H, D = 64, 128
         if self.causal:
@@ -528,8 +528,8 @@ class IndexWorkload(Workload):
                     ok = ok and torch.equal(ri, idx[:, r0:r0 + 8]) and torch.equal(rv, vals[:, r0:r0 + 8])
                 del kd, ksd
             out["parity_ok"] = bool(ok)
-            out["parity_note"] = ("merged selection of query rows 0-7 and 4088-4095 equals (indices and values) a "
-                                  "one-GPU int8_index_topk over all 131072 keys")
+            out["parity_note"] = (f"merged selection of query rows 0-7 and {self.M - 8}-{self.M - 1} equals (indices "
+                                  f"and values) a one-GPU int8_index_topk over all {self.N} keys")
         return out
 
     def cpu_sample(self, seconds):
@@ -743,8 +743,10 @@ def make_workload(name, args, rank, world):
         return ActQuantWorkload(2048, 7168, args.aq_dtype, rank, world)
     if name in ("act_quant_fp32", "act_quant_bf16"):
         return ActQuantWorkload(2048, 7168, name.split("_")[-1], rank, world)
-    if name in ("index_prefill", "index_decode", "index_long"):
+    if name in ("index_prefill", "index_decode"):
         return IndexWorkload(name.split("_")[1], rank, world)
+    if name == "index_long":
+        return IndexWorkload("long", rank, world, queries=args.long_queries)
     if name in ("rotate_quant", "weight_quant"):
         return ProducerWorkload(name, rank, world)
     if name == "index_step":
@@ -980,6 +982,8 @@ def main():
                     choices=["gemm_up", "gemm_down", "act_quant", "index_prefill", "index_decode", "index_long",
                              "rotate_quant", "weight_quant", "index_step"])
     ap.add_argument("--m", type=int, default=32, help="M for gemm_down")
+    ap.add_argument("--long-queries", type=int, default=4096,
+                    help="query rows of index_long (4096 = BASELINE's config; fewer for profiler captures)")
     ap.add_argument("--out", default="bf16", choices=["bf16", "fp32"], help="output dtype for gemm_down")
     ap.add_argument("--aq-dtype", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

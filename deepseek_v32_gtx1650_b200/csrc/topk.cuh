@@ -780,19 +780,21 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int cnt = __popc(mask);
     const int off = excl_scan_once<THREADS>(cnt, sh.scan);
     if (tid == THREADS - 1) sh.total = off + cnt;
+    // This thread's candidates, lowest position first: one pass per candidate (a few % of the
+    // positions), not a branch per position; the value is re-read (an L1 hit).
     int o = running + off;
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      if (mask & (1u << i)) {
-        if (o < cap) {
-          ci[o] = cin ? cin[p + i] : static_cast<int32_t>(p + i + idx_offset);
-          cv[o] = __uint_as_float(key[i]);
-        }
-        ++o;
+    while (mask) {
+      const int i = __ffs(mask) - 1;
+      mask &= mask - 1;
+      if (o < cap) {
+        ci[o] = cin ? cin[p + i] : static_cast<int32_t>(p + i + idx_offset);
+        cv[o] = __ldg(v + p + i);
       }
+      ++o;
     }
     __syncthreads();
     running += sh.total;
+    if (running > cap) break;  // (block-uniform) the list overflows: the row takes the fallback
   }
   if (tid == 0) cand_n[r] = (running >= k && running <= cap) ? running : kRowFallback;
 }

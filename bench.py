@@ -475,10 +475,12 @@ class IndexWorkload(Workload):
 
     def roofline(self, kernel_ms, peaks, src, traffic):
         peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        share = (self.world * 4096 / self.M) if self.kind == "long" else 1
         ops = self.ops / (self.world if self.kind == "long" else 1)
         ach = ops / (kernel_ms * 1e-3) / 1e12
+        tr = traffic.get(self.name)  # (the long case's figure is one GPU's 4096-query launch)
         return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
-                "frac": round(ach / peak, 4), "traffic": traffic.get(self.name),
+                "frac": round(ach / peak, 4), "traffic": None if tr is None else int(tr / share),
                 "peak_note": f"dense INT8 = 2 x {src} cuBLAS bf16 burst; achieved counts visible (query, key) "
                              f"pairs only, for the indexer kernel alone", "ops_per_launch": ops,
                 "full_mn_convention_tops": round(self.ops_full / (self.world if self.kind == 'long' else 1)

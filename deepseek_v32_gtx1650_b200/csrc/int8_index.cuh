@@ -15,8 +15,9 @@
 // one is still in the epilogue).
 //   warps 0-15  epilogue: each thread owns one key and reduces relu(logit) * w over the heads of
 //               its queries entirely in registers (no cross-lane reduction), then scales by k_s and
-//               stores. Warp w reads TMEM lanes 32*(w%4).. and column quarter w/4 (QB/4 queries);
-//               four epilogue warps per SM sub-partition hide the TMEM load latency.
+//               stores. Two groups of eight warps take alternate key tiles (group g reads TMEM buffer
+//               g), so one group computes while the other waits for its accumulator; in a group, warp
+//               w reads TMEM lanes 32*(w%4).. and column half (w/4)%2 (QB/2 queries) in two passes.
 //   warp 16     TMA producer: the unit's Q block into one of two Q buffers, then its key tiles
 //               into a 4-stage ring.
 //   warp 17     MMA issuer: D / 32 MMAs per key tile into one of two int32 TMEM accumulators.
@@ -59,8 +60,9 @@ struct Cfg {
   static constexpr int QB = kNmma / H;                 // queries per block
   static constexpr int kQBytes = QB * H * D;           // Q tile bytes
   static constexpr int kKBytes = kKeysPerTile * D;     // key tile bytes per stage
-  static constexpr int kColsPerWarp = kNmma / 4;      // columns per epilogue warp (one quarter)
-  static constexpr int kQPerWarp = QB / 4;            // queries per epilogue warp
+  static constexpr int kColsPerWarp = kNmma / 2;      // columns per epilogue warp (one half)
+  static constexpr int kQPerWarp = QB / 2;            // queries per epilogue warp
+  static constexpr int kQPerPass = kQPerWarp / 2;     // queries per 64-column pass of a warp
   static constexpr int kOffQ = 0;                      // two Q buffers
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffW = kOffK + kStages * kKBytes;  // per epilogue warp: its half's weights
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(qfull_bar(b), 1);
       mbar_init(qempty_bar(b), 1);
       mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), kEpiWarps);
+      mbar_init(tempty_bar(b), kEpiWarps / 2);  // the epilogue group that reads buffer b
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(kfull_bar(s), 1);
@@ -295,25 +297,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < kEpiWarps) {
-    // ------------------------------------------------------------ epilogue (512 threads)
-    const int wq = warp & 3;   // TMEM lane quarter (keys)
-    const int wc = warp >> 2;  // column quarter (queries)
-    const int q_first = wc * C::kQPerWarp;  // first query (within the block) of this warp
-    const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(wc * C::kColsPerWarp);
+    // ------------------------------------------------------------ epilogue (two groups of 8 warps)
+    // Group g reads TMEM buffer g, i.e. the key tiles i (counted over all units of this CTA) with
+    // i % 2 == g; while one group waits for its next accumulator the other computes. In a group, warp
+    // (wq, ch) reads lane quarter wq (keys) and column half ch (QB / 2 queries) in two passes of 64
+    // columns, releasing the buffer after the second pass's TMEM read.
+    const int g = warp >> 3;
+    const int wq = warp & 3;   // TMEM lane quarter (keys); a warp reads lanes 32 * (warp % 4) ..
+    const int ch = (warp >> 2) & 1;
+    const int q_first = ch * C::kQPerWarp;  // first query (within the block) of this warp
+    const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(g * kNmma + ch * C::kColsPerWarp);
     float* sWw = reinterpret_cast<float*>(smem + C::kOffW) + warp * C::kColsPerWarp;  // this warp's copy
     const float4* w4p = reinterpret_cast<const float4*>(sWw);
     bool ok = true;
-    __syncwarp();  // both accumulators start free
-    if (lane == 0) {
-      mbar_arrive(tempty_bar(0));
-      mbar_arrive(tempty_bar(1));
-    }
-    uint32_t i = 0;
+    __syncwarp();  // this group's accumulator starts free
+    if (lane == 0) mbar_arrive(tempty_bar(g));
+    const int n_base = wq * 32 + lane;
+    uint32_t i = 0;  // key tiles of all units so far (both groups)
     for (int r = 0; ok; ++r) {
       const int idx = unit_of_round(r, units);
       if (idx < 0) break;
       const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
       if (un.kt_vis == un.kt0) continue;
+      const uint32_t i0 = i;
+      i += static_cast<uint32_t>(un.kt_vis - un.kt0);
+      const int kt_first = un.kt0 + static_cast<int>((static_cast<uint32_t>(g) - i0) & 1u);
+      if (kt_first >= un.kt_vis) continue;  // the unit's only tile is the other group's
+      uint32_t kk = (i0 + (g == 0 ? 1u : 0u)) >> 1;  // this group's tiles before this unit
       // Head weights of this warp's queries (rows past M read as 0): a private copy per warp,
       // so no barrier across warps is needed.
       __syncwarp();
@@ -322,86 +332,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         sWw[e] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (e % H)) : 0.f;
       }
       __syncwarp();
-      // Per unit: this thread's key column, its k_s and output pointers, and per query the last
-      // visible tile offset (so the per-tile work has no 64-bit arithmetic).
-      const int n_base = wq * 32 + lane;
+      // Per unit: this thread's key column and its k_s, the first query's output row and, for
+      // causal rows, the last visible tile offset of the first query (query q: lim0 + q).
+      const int m_first = un.m0 + q_first;
       const float* ksp = k_s + static_cast<int64_t>(un.b) * ks_ld + n_base;
-      float* outp[C::kQPerWarp];
-      int lim[C::kQPerWarp];  // the key of tile offset t is visible to query q iff t <= lim[q]
+      float* out0 = out + (static_cast<int64_t>(un.b) * M + m_first) * N + n_base;
+      const long long l0 = causal ? start + m_first - n_base : (1LL << 30);
+      const int lim0 = static_cast<int>(l0 < -(1LL << 30) ? -(1LL << 30) : (l0 > (1LL << 30) ? (1LL << 30) : l0));
       // Rows selected here (m < m_triv: at most sel_k visible keys) have their scores written only
       // when kept as output. sel_unit (warp-uniform): some query of this warp is such a row.
-      const bool sel_unit = kSel && un.m0 + q_first < m_triv;
-#pragma unroll
-      for (int q = 0; q < C::kQPerWarp; ++q) {
-        const int m = un.m0 + q_first + q;
-        outp[q] = (m < M && (fill_masked || !kSel || m >= m_triv))
-                      ? out + (static_cast<int64_t>(un.b) * M + m) * N + n_base
-                      : nullptr;
-        const long long l = causal ? start + m - n_base : 0x7FFFFFFFLL;
-        lim[q] = static_cast<int>(l < -1 ? -1 : (l > 0x7FFFFFFFLL ? 0x7FFFFFFFLL : l));
-      }
-      // k_s of this thread's key in the next tile, loaded a tile ahead (its latency stalled the
-      // epilogue of long rows: 1024 x 131072 keys 2.03 -> 1.98 ms).
-      float ks_next = (un.kt0 * kKeysPerTile + n_base < N) ? __ldg(ksp + un.kt0 * kKeysPerTile) : 0.f;
-      for (int kt = un.kt0; kt < un.kt_vis; ++kt, ++i) {
-        const uint32_t buf = i & 1u;
+      const bool sel_unit = kSel && m_first < m_triv;
+      // k_s of this thread's key in this group's next tile, loaded a tile ahead.
+      float ks_next = (kt_first * kKeysPerTile + n_base < N) ? __ldg(ksp + kt_first * kKeysPerTile) : 0.f;
+      for (int kt = kt_first; kt < un.kt_vis; kt += 2, ++kk) {
         const int toff = kt * kKeysPerTile;
         const bool n_ok = toff + n_base < N;
         // k_s * 2^22 undoes the 2^-22 of the relu step (power-of-two scalings: same rounding).
         const float ks = ks_next * 0x1p22f;
-        ks_next = (kt + 1 < un.kt_vis && toff + kKeysPerTile + n_base < N) ? __ldg(ksp + toff + kKeysPerTile) : 0.f;
-        if (!mbar_wait_warp(tfull_bar(buf), (i >> 1) & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
+        ks_next = (kt + 2 < un.kt_vis && toff + 2 * kKeysPerTile + n_base < N) ? __ldg(ksp + toff + 2 * kKeysPerTile)
+                                                                               : 0.f;
+        if (!mbar_wait_warp(tfull_bar(g), kk & 1u, abort_flag, (KID_INDEX << 16) | 5)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // Both 32-column chunks of this warp's quarter in flight at once, then one wait.
-        const uint32_t tb = t_lane + buf * kNmma;
-        uint32_t ra[32], rb[32];
-        tmem_ld32_async(tb, ra);
-        tmem_ld32_async(tb + 32, rb);
-        tmem_wait_ld32(ra);
-        tmem_wait_ld32(rb);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar(buf));  // the accumulator is in registers now
-        // Two accumulators per query (even / odd column pairs) halve the FMA dependency chain.
-        float2 acc[C::kQPerWarp][2];
 #pragma unroll
-        for (int q = 0; q < C::kQPerWarp; ++q) acc[q][0] = acc[q][1] = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t(&rr)[32] = c ? rb : ra;
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 w4 = w4p[c * 8 + j4];     // same address across the warp: broadcast
-            const int q = (c * 32 + 4 * j4) / H;  // query of these 4 columns (compile time)
-            const float2 v0 = make_float2(relu_i32_x2m22(rr[4 * j4]), relu_i32_x2m22(rr[4 * j4 + 1]));
-            const float2 v1 = make_float2(relu_i32_x2m22(rr[4 * j4 + 2]), relu_i32_x2m22(rr[4 * j4 + 3]));
-            acc[q][0] = __ffma2_rn(v0, make_float2(w4.x, w4.y), acc[q][0]);
-            acc[q][1] = __ffma2_rn(v1, make_float2(w4.z, w4.w), acc[q][1]);
+        for (int pass = 0; pass < 2; ++pass) {
+          // Both 32-column chunks of this pass in flight at once, then one wait.
+          uint32_t ra[32], rb[32];
+          tmem_ld32_async(t_lane + pass * 64, ra);
+          tmem_ld32_async(t_lane + pass * 64 + 32, rb);
+          tmem_wait_ld32(ra);
+          tmem_wait_ld32(rb);
+          if (pass == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(g));  // the accumulator is in registers now
           }
-        }
-        if (n_ok && !sel_unit) {
+          // Two accumulators per query (even / odd column pairs) halve the FMA dependency chain.
+          float2 acc[C::kQPerPass][2];
 #pragma unroll
-          for (int q = 0; q < C::kQPerWarp; ++q) {
-            if (outp[q]) {
-              float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
-              if (toff > lim[q]) sc = -INFINITY;
-              outp[q][toff] = sc;
+          for (int q = 0; q < C::kQPerPass; ++q) acc[q][0] = acc[q][1] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t(&rr)[32] = c ? rb : ra;
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 w4 = w4p[pass * 16 + c * 8 + j4];  // same address across the warp: broadcast
+              const int q = (c * 32 + 4 * j4) / H;             // query of these 4 columns in the pass
+              const float2 v0 = make_float2(relu_i32_x2m22(rr[4 * j4]), relu_i32_x2m22(rr[4 * j4 + 1]));
+              const float2 v1 = make_float2(relu_i32_x2m22(rr[4 * j4 + 2]), relu_i32_x2m22(rr[4 * j4 + 3]));
+              acc[q][0] = __ffma2_rn(v0, make_float2(w4.x, w4.y), acc[q][0]);
+              acc[q][1] = __ffma2_rn(v1, make_float2(w4.z, w4.w), acc[q][1]);
             }
           }
-        } else if (kSel && n_ok) {
+          if (n_ok) {
 #pragma unroll
-          for (int q = 0; q < C::kQPerWarp; ++q) {
-            float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
-            if (toff > lim[q]) sc = -INFINITY;
-            if (outp[q]) outp[q][toff] = sc;
-            const int m = un.m0 + q_first + q;
-            if (m < m_triv && toff + n_base < sel_k) {  // output j of such a row is position j
-              const int64_t so = (static_cast<int64_t>(un.b) * M + m) * sel_k + toff + n_base;
-              sel_val[so] = sc;
-              sel_idx[so] = toff + n_base + key_offset;
+            for (int q = 0; q < C::kQPerPass; ++q) {
+              const int qw = pass * C::kQPerPass + q;  // query within the warp
+              const int m = m_first + qw;
+              float sc = ((acc[q][0].x + acc[q][0].y) + (acc[q][1].x + acc[q][1].y)) * ks;
+              if (toff > lim0 + qw) sc = -INFINITY;
+              if (!sel_unit) {
+                if (m < M) out0[static_cast<int64_t>(qw) * N + toff] = sc;
+              } else if (kSel) {
+                if (m < M && (fill_masked || m >= m_triv)) out0[static_cast<int64_t>(qw) * N + toff] = sc;
+                if (m < m_triv && toff + n_base < sel_k) {  // output j of such a row is position j
+                  const int64_t so = (static_cast<int64_t>(un.b) * M + m) * sel_k + toff + n_base;
+                  sel_val[so] = sc;
+                  sel_idx[so] = toff + n_base + key_offset;
+                }
+              }
             }
           }
         }

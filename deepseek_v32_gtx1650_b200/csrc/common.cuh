@@ -320,6 +320,14 @@ DSV32_DEV float relu_i32_x2m22(uint32_t bits) {
   return r;
 }
 
+// 16-byte asynchronous copy global -> shared (no registers held while in flight); src_bytes = 0
+// zero-fills the destination without reading. Completion: cp_async_wait_all() by the issuing thread.
+DSV32_DEV void cp_async16(uint32_t smem_dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_dst), "l"(src), "r"(src_bytes) : "memory");
+}
+DSV32_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+DSV32_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Width-generic forms of the pipelined TMEM reads (16 or 32 columns).
 template <int W>
 DSV32_DEV void tmem_ld_async(uint32_t taddr, uint32_t (&r)[W]) {

@@ -394,7 +394,7 @@ int index_impl(const int8_t* q, const float* w, const int8_t* k, const float* k_
   if (!((heads == 16 || heads == 32 || heads == 64) && (dim == 64 || dim == 128))) return DSV32_ERR_UNSUPPORTED;
   // (keys stay below 2^30: the epilogue's per-query visibility bounds are kept within +-2^30)
   if (m * heads > (1LL << 31) - 1 || n >= (1LL << 30) || batch > 65535) return DSV32_ERR_UNSUPPORTED;
-  if (!aligned16(q) || !aligned16(k)) return DSV32_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(w)) return DSV32_ERR_INVALID_ARG;
   int dev = 0;
   DeviceInfo* info = nullptr;
   if (int st = device_setup(&dev, &info)) return st;

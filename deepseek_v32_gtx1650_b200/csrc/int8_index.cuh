@@ -65,8 +65,9 @@ struct Cfg {
   static constexpr int kQPerPass = kQPerWarp / 2;     // queries per 64-column pass of a warp
   static constexpr int kOffQ = 0;                      // two Q buffers
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
-  static constexpr int kOffW = kOffK + kStages * kKBytes;  // per epilogue warp: its half's weights
-  static constexpr int kOffBar = kOffW + kEpiWarps * kColsPerWarp * 4;
+  static constexpr int kOffW = kOffK + kStages * kKBytes;  // per epilogue warp: two units' weights
+  static constexpr int kOffBar = kOffW + kEpiWarps * 2 * kColsPerWarp * 4;
+  static_assert(kColsPerWarp == 32 * 4, "one 16-byte copy per lane per unit's weights");
   // qfull[2], qempty[2], kfull[kStages], kempty[kStages], tfull[2], tempty[2], mma_done
   static constexpr int kNumBars = 9 + 2 * kStages;
   static constexpr int kOffTmem = kOffBar + 8 * kNumBars;
@@ -307,16 +308,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ch = (warp >> 2) & 1;
     const int q_first = ch * C::kQPerWarp;  // first query (within the block) of this warp
     const uint32_t t_lane = tmem_base + (uint32_t(wq * 32) << 16) + uint32_t(g * kNmma + ch * C::kColsPerWarp);
-    float* sWw = reinterpret_cast<float*>(smem + C::kOffW) + warp * C::kColsPerWarp;  // this warp's copy
-    const float4* w4p = reinterpret_cast<const float4*>(sWw);
+    float* sWw = reinterpret_cast<float*>(smem + C::kOffW) + warp * 2 * C::kColsPerWarp;  // this warp's
+    const float4* w4p = reinterpret_cast<const float4*>(sWw);  // the half the tile loop reads
     bool ok = true;
     __syncwarp();  // this group's accumulator starts free
     if (lane == 0) mbar_arrive(tempty_bar(g));
     const int n_base = wq * 32 + lane;
+    // Head weights of this warp's queries in the unit of round rr (its QB / 2 rows of w, contiguous;
+    // rows past M zero-filled) into the staging half of the warp's private copy, one unit ahead, as
+    // asynchronous copies (one 16-byte copy per lane, no registers held while in flight): their
+    // latency falls inside the previous unit. At a unit's start each lane moves its 16 bytes to the
+    // half the tile loop reads, which keeps that loop's addresses fixed. (Weights loaded into
+    // registers a unit ahead instead cost the long-row loop 8 %; reading the two halves
+    // alternately, 3 %.)
+    auto fetch_w = [&](int rr) {
+      const int idx = unit_of_round(rr, units);
+      if (idx < 0) return;
+      const Unit u = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
+      const int e = lane * 4;
+      const int m = u.m0 + q_first + e / H;
+      const float* src = (m < M) ? w + (static_cast<int64_t>(u.b) * M + m) * H + (e % H) : w;
+      cp_async16(smem_u32(sWw + C::kColsPerWarp + e), src, m < M ? 16u : 0u);
+      cp_async_commit();
+    };
+    fetch_w(0);
     uint32_t i = 0;  // key tiles of all units so far (both groups)
     for (int r = 0; ok; ++r) {
       const int idx = unit_of_round(r, units);
       if (idx < 0) break;
+      // Round r's weights have landed in the staging half: each lane moves its own 16 bytes (its
+      // copies are complete once it has waited), the warp barrier orders round r - 1's reads of the
+      // loop half before, and every lane's move before round r's reads and the next copy.
+      cp_async_wait_all();
+      __syncwarp();
+      reinterpret_cast<float4*>(sWw)[lane] = reinterpret_cast<const float4*>(sWw + C::kColsPerWarp)[lane];
+      __syncwarp();
+      fetch_w(r + 1);
       const Unit un = decode_unit(idx, M, N, C::QB, causal, start, tiles_per_chunk, num_chunks);
       if (un.kt_vis == un.kt0) continue;
       const uint32_t i0 = i;
@@ -324,14 +351,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kt_first = un.kt0 + static_cast<int>((static_cast<uint32_t>(g) - i0) & 1u);
       if (kt_first >= un.kt_vis) continue;  // the unit's only tile is the other group's
       uint32_t kk = (i0 + (g == 0 ? 1u : 0u)) >> 1;  // this group's tiles before this unit
-      // Head weights of this warp's queries (rows past M read as 0): a private copy per warp,
-      // so no barrier across warps is needed.
-      __syncwarp();
-      for (int e = lane; e < C::kColsPerWarp; e += 32) {
-        const int m = un.m0 + q_first + e / H;
-        sWw[e] = (m < M) ? __ldg(w + (static_cast<int64_t>(un.b) * M + m) * H + (e % H)) : 0.f;
-      }
-      __syncwarp();
       // Per unit: this thread's key column and its k_s, the first query's output row and, for
       // causal rows, the last visible tile offset of the first query (query q: lim0 + q).
       const int m_first = un.m0 + q_first;
@@ -408,6 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    cp_async_wait_all();  // a weight copy issued before an abort lands before the CTA can exit
   }
 
   tc_fence_before();

@@ -450,11 +450,14 @@ constexpr int kTopkRegMax = 512 * 16;                       // longest row a reg
 constexpr int64_t kTopkPreferredBytes = int64_t(256) << 20;  // workspace the library asks for, at most
 
 // Long-row filter (topk_filter_kernel): plain rows longer than one register pass, k small enough
-// that a list of 3 k candidates fits one register pass, and at least as many rows as SMs (with fewer
+// that a list of 2 k candidates fits one register pass, and at least as many rows as SMs (with fewer
 // rows the staged plan, which spreads each row's segments over several CTAs, is faster).
 constexpr int kTopkFilterMinN = kTopkRegMax;
-bool filter_shape(int64_t n, int64_t k) { return n > kTopkFilterMinN && 3 * k <= kTopkRegMax; }
-int filter_cap(int k) { return (3 * k + 15) / 16 * 16; }
+bool filter_shape(int64_t n, int64_t k) { return n > kTopkFilterMinN && 2 * k <= kTopkRegMax; }
+// List capacity 2 k: a list of at most 4096 candidates (k = 2048) is selected by the 256-thread
+// register kernel, six CTAs per SM (3 k lists took the 512-thread one; with the 1.4 k target, random
+// rows 4096 x 16384 368 -> 301 us, 2048 x 131072 364 -> 331 us).
+int filter_cap(int k) { return (2 * k + 15) / 16 * 16; }
 int64_t filter_per_row(int k) { return int64_t(filter_cap(k)) * 8 + 16; }
 
 // Stage plan for rows longer than one register pass: each row is cut into equal segments of at most
@@ -552,9 +555,14 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
     for (int64_t r0 = 0; r0 < rows; r0 += fb) {
       const int64_t rb = std::min<int64_t>(rows - r0, fb);
       const int32_t* cin = cand_idx ? cand_idx + r0 * cand_ld : nullptr;
-      if (int rc = launch(topk_filter_kernel<kFilterThreads, kFilterItems>, static_cast<unsigned>(rb),
-                          kFilterThreads, 0, st, "topk filter kernel launch", scores + r0 * ld, ld, nn, cin, cand_ld,
-                          idx_offset, kk, cm, cs, static_cast<long long>(r0), ci, cv, cn, cap))
+      const bool short_rows = nn <= kFilterShortN;
+      if (int rc = short_rows ? launch(topk_filter_kernel<256, kFilterItems>, static_cast<unsigned>(rb), 256, 0, st,
+                                       "topk filter kernel launch", scores + r0 * ld, ld, nn, cin, cand_ld, idx_offset,
+                                       kk, cm, cs, static_cast<long long>(r0), ci, cv, cn, cap)
+                              : launch(topk_filter_kernel<kFilterThreads, kFilterItems>, static_cast<unsigned>(rb),
+                                       kFilterThreads, 0, st, "topk filter kernel launch", scores + r0 * ld, ld, nn,
+                                       cin, cand_ld, idx_offset, kk, cm, cs, static_cast<long long>(r0), ci, cv, cn,
+                                       cap))
         return rc;
       if (int rc = topk_reg_launch(cv, rb, cap, cap, ci, cap, 0, kk, out_idx + r0 * k, out_val + r0 * k, 0, 0, 0, cap,
                                    1, st, RowParts{}, cn))

@@ -615,8 +615,8 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
 // ---------------------------------------------------------------------------- long rows: filter
 // Rows much longer than one register pass (the long-context indexer: 131072 keys) are reduced to a
 // short candidate list in one read: a sample of the row gives a threshold T whose expected count of
-// keys >= T is about 1.5 k; one pass over the row writes every key >= T, in position order, with its
-// id, to the row's candidate list (at most `cap` = 3 k entries); the register kernel then selects the
+// keys >= T is about 1.4 k; one pass over the row writes every key >= T, in position order, with its
+// id, to the row's candidate list (at most `cap` = 2 k entries); the register kernel then selects the
 // k largest of the list (row_len = its length). Every key >= the row's k-th largest is in the list
 // whenever the list holds at least k keys, so the selection, ties included, equals the one over the
 // whole row. A row whose list would hold fewer than k keys or more than cap (a sample far from the
@@ -624,26 +624,60 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
 // marked kRowFallback and selected by topk_gmem_kernel instead. One CTA per row.
 constexpr int kFilterThreads = 512;
 constexpr int kFilterItems = 16;
+// Rows of at most this many keys use 256-thread CTAs (four per SM, a 4096-key sample): their fixed
+// per-row work (sample, threshold search, barriers) weighs more, and more CTAs per SM hide it (random
+// rows 4096 x 16384 301 -> 229 us, 4096 x 32768 -> 279 us, 2048 x 65536 235 -> 197 us). Longer rows keep
+// 512 threads: with a 4096-key sample the threshold's error sends rows of 131072 to the fallback.
+constexpr int kFilterShortN = 65536;
 
 struct FilterShared {
   int hist[1 << kRegBits];
   int scan[32];
-  uint32_t prefix;
-  int krem, total;
+  uint32_t red[2][32];  // per-warp minimum / maximum key
+  uint32_t cand[32];    // keys of the last open histogram bin (at most 32)
+  uint32_t prefix, T;
+  int krem, total, bin_cnt, cand_n;
 };
 
 // The c-th largest (1-based) key held by the block (ITEMS per thread; key 0 = no key), for
-// 1 <= c <= number of keys: up to three 11-bit histogram passes over the keys matching the prefix.
+// 1 <= c <= number of keys. The bits common to the smallest and largest key are skipped (scores of
+// one row share their sign and often their exponent), then 11-bit histogram passes over the keys
+// matching the prefix found so far; as soon as the open bin holds at most 32 keys one warp ranks them.
 template <int THREADS, int ITEMS>
 DSV32_DEV uint32_t block_kth_key(const uint32_t (&key)[ITEMS], int c, FilterShared& sh) {
-  uint32_t prefix = 0;
-  int shift = 32;
+  constexpr int W = THREADS / 32;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  {
+    uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+      if (key[i] != 0u) {
+        mn = min(mn, key[i]);
+        mx = max(mx, key[i]);
+      }
+    }
+    mn = __reduce_min_sync(0xffffffffu, mn);
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if (lane == 0) {
+      sh.red[0][wid] = mn;
+      sh.red[1][wid] = mx;
+    }
+  }
+  __syncthreads();
+  uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    mn = min(mn, sh.red[0][w]);
+    mx = max(mx, sh.red[1][w]);
+  }
+  int shift = (mn == mx) ? 0 : 32 - __clz(mn ^ mx);  // bits [shift, 32) common to every key
+  uint32_t prefix = (shift >= 32) ? 0u : (mx & ~((1u << shift) - 1u));
   while (shift > 0) {
     const int d = min(kRegBits, shift);
     const int nbins = 1 << d;
     const int ns = shift - d;
     for (int i = threadIdx.x; i < nbins; i += THREADS) sh.hist[i] = 0;
-    __syncthreads();
+    __syncthreads();  // (also orders the statistics' reads above and the previous pass's reads)
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i)
       if (key[i] != 0u && prefix_match(key[i], prefix, shift)) atomicAdd(&sh.hist[(key[i] >> ns) & (nbins - 1)], 1);
@@ -663,6 +697,8 @@ DSV32_DEV uint32_t block_kth_key(const uint32_t (&key)[ITEMS], int c, FilterShar
         if (acc + cnt >= c) {
           sh.prefix = prefix | (uint32_t(bin) << ns);
           sh.krem = c - acc;
+          sh.bin_cnt = cnt;
+          sh.cand_n = 0;
           break;
         }
         acc += cnt;
@@ -672,6 +708,27 @@ DSV32_DEV uint32_t block_kth_key(const uint32_t (&key)[ITEMS], int c, FilterShar
     prefix = sh.prefix;
     c = sh.krem;
     shift = ns;
+    const int cnt = sh.bin_cnt;
+    if (shift > 0 && cnt <= 32) {
+      // At most a warp's worth of keys share the digits found so far: one warp ranks them.
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i)
+        if (key[i] != 0u && prefix_match(key[i], prefix, shift)) sh.cand[atomicAdd(&sh.cand_n, 1)] = key[i];
+      __syncthreads();
+      if (wid == 0) {
+        const uint32_t mine = lane < cnt ? sh.cand[lane] : 0u;
+        int g = 0, e = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const uint32_t o = __shfl_sync(0xffffffffu, mine, j);
+          g += (j < cnt && o > mine) ? 1 : 0;
+          e += (j < cnt && o == mine) ? 1 : 0;
+        }
+        if (lane < cnt && g < c && c <= g + e) sh.T = mine;  // every holder of this key writes it
+      }
+      __syncthreads();
+      return sh.T;
+    }
     __syncthreads();  // the next pass clears the histogram the scan above read
   }
   return prefix;
@@ -702,7 +759,7 @@ DSV32_DEV void load_bits(const float* v, int p, int valid, uint32_t (&bits)[ITEM
 // p + idx_offset. Output: the row's list in cand_idx / cand_val[r * cap ..], its length in cand_n[r]
 // (kRowFallback when the list does not apply).
 template <int THREADS, int ITEMS>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, THREADS == 256 ? 4 : 2)
     topk_filter_kernel(const float* __restrict__ vals, long long ld, int n, const int32_t* __restrict__ cand_in,
                        long long cand_in_ld, long long idx_offset, int k, int causal_m, long long causal_start,
                        long long causal_row0, int32_t* __restrict__ cand_idx, float* __restrict__ cand_val,
@@ -742,9 +799,9 @@ __global__ void __launch_bounds__(THREADS, 2)
     for (int w = 0; w < THREADS / 32; ++w) s_n += sh.scan[w];
     __syncthreads();
   }
-  // 2. Threshold: the c-th largest sampled key, c scaled so that about 1.5 k keys of the row reach it
+  // 2. Threshold: the c-th largest sampled key, c scaled so that about 1.4 k keys of the row reach it
   //    (exactly the k-th largest when the sample is the whole row). valid > k >= 1, so s_n >= 1.
-  long long c_ll = (s_n >= valid) ? k : (3LL * k * s_n + 2LL * valid - 1) / (2LL * valid);
+  long long c_ll = (s_n >= valid) ? k : (7LL * k * s_n + 5LL * valid - 1) / (5LL * valid);
   if (c_ll < 1) c_ll = 1;
   if (c_ll > s_n) c_ll = s_n;
   const uint32_t T = block_kth_key<THREADS, ITEMS>(key, static_cast<int>(c_ll), sh);

@@ -215,3 +215,107 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
 }
 
 }  // namespace dsv32
+
+namespace dsv32 {
+
+// ---------------------------------------------------------------- 16-bit input (bf16 / fp16)
+// Same results as act_quant_kernel, computed without the near-tie test. 16-bit inputs are full of
+// exact and near rounding ties (a value equal to amax / 2 gives x / s = 63.5 up to the rounding of s:
+// about a third of the groups of normal bf16 data hold one), so the fast-path-plus-fix-up form ran
+// its exact path in most warp iterations. Here every value takes one exact path with no branch:
+// with z = RN(1/s) (the correctly rounded reciprocal, once per group) and y = RN(x * z),
+//   q = RN(y + RN(x - y * s) * z) = RN(x / s)
+// (Markstein's theorem: y is within one ulp of x / s, so the remainder x - y * s is exact in one
+// FMA, and one correction with a correctly rounded reciprocal gives the correctly rounded
+// quotient; valid without overflow or underflow, which |q| <= 127.x and s >= 1e-4 / 127 rule out).
+// Then RN(q + 1.5 * 2^23) rounds q to an integer, ties to even, and its low byte is the int8.
+// Per pair of values: one packed multiply, two packed FMAs, one packed add. A group holding an
+// infinity or NaN (scale not finite) takes the IEEE division per value (aq_exact_bits: NaN -> 0).
+// Layout: one 128-value group per 16 lanes (8 values per lane, one 16-byte load), two groups per
+// warp slot, UNROLL consecutive slots per warp iteration; iterations whose slots are all complete
+// run without validity tests, their loads and stores at constant offsets from one base pointer.
+
+template <bool kRound>
+DSV32_DEV float aq_scale_t(float amax) {
+  return aq_scale(amax, kRound);
+}
+
+template <typename T, bool kRound>
+DSV32_DEV void aq16_slot(const uint4& raw, uint2& out, float& sc) {
+  float f[8];
+  to_f32(raw, f, static_cast<T*>(nullptr));
+  float a = max_nan(max_nan(max_nan(fabsf(f[0]), fabsf(f[1])), max_nan(fabsf(f[2]), fabsf(f[3]))),
+                    max_nan(max_nan(fabsf(f[4]), fabsf(f[5])), max_nan(fabsf(f[6]), fabsf(f[7]))));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
+  sc = aq_scale_t<kRound>(max_nan(a, 1e-4f));  // NaN anywhere in the group -> NaN
+  constexpr float kMagic = 12582912.0f;
+  uint32_t q[8];
+  if (sc < INFINITY) {
+    const float z = __frcp_rn(sc);
+    const float2 z2 = make_float2(z, z), ns2 = make_float2(-sc, -sc), m2 = make_float2(kMagic, kMagic);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float2 x2 = make_float2(f[e], f[e + 1]);
+      const float2 y = __fmul2_rn(x2, z2);
+      const float2 r = __ffma2_rn(y, ns2, x2);      // x - y * s, exact
+      const float2 qq = __ffma2_rn(r, z2, y);       // RN(x / s)
+      const float2 big = __fadd2_rn(qq, m2);        // rint, ties to even, + 1.5 * 2^23
+      q[e] = __float_as_uint(big.x);
+      q[e + 1] = __float_as_uint(big.y);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = __float_as_uint(aq_exact_bits(f[e], sc));
+  }
+  out = make_uint2(aq_pack4(q[0], q[1], q[2], q[3]), aq_pack4(q[4], q[5], q[6], q[7]));
+}
+
+template <typename T, bool kRound, int UNROLL>
+__global__ void __launch_bounds__(256) act_quant16_kernel(const T* __restrict__ x, int8_t* __restrict__ y,
+                                                          float* __restrict__ s, int64_t num_groups) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 4;  // group of the slot
+  const int sl = lane & 15;   // lane within the group
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t full_slots = num_groups >> 1;  // slots holding two groups
+  pdl_wait();
+  pdl_launch_dependents();
+
+  int64_t base = warp * UNROLL;
+  for (; base + UNROLL <= full_slots; base += nwarps * UNROLL) {
+    const int64_t g0 = base * 2 + sub;  // this lane's group in slot 0; slot u is 2u groups further
+    const uint4* src = reinterpret_cast<const uint4*>(x + g0 * 128 + sl * 8);
+    uint4 raw[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) raw[u] = __ldcs(src + u * 32);
+    uint2 out[UNROLL];
+    float sc[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) aq16_slot<T, kRound>(raw[u], out[u], sc[u]);
+    uint2* dst = reinterpret_cast<uint2*>(y + g0 * 128 + sl * 8);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) __stcs(dst + u * 32, out[u]);
+    if (sl == 0) {
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) s[g0 + 2 * u] = sc[u];
+    }
+  }
+  // The warp's last, incomplete iteration (and an odd last group): one slot at a time, checked.
+  const int64_t slots = (num_groups + 1) >> 1;
+  for (int64_t sb = base; sb < base + UNROLL && sb < slots; ++sb) {
+    const int64_t g = sb * 2 + sub;
+    const bool valid = g < num_groups;
+    const uint4 raw = valid ? __ldcs(reinterpret_cast<const uint4*>(x + g * 128 + sl * 8)) : make_uint4(0u, 0u, 0u, 0u);
+    uint2 out;
+    float sc;
+    aq16_slot<T, kRound>(raw, out, sc);
+    if (valid) {
+      __stcs(reinterpret_cast<uint2*>(y + g * 128 + sl * 8), out);
+      if (sl == 0) s[g] = sc;
+    }
+  }
+}
+
+}  // namespace dsv32

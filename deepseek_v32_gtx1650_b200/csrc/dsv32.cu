@@ -116,12 +116,11 @@ int device_setup(int* dev_out, DeviceInfo** info_out) {
         DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
             &nb, act_quant_kernel<float, kAqEplF32, kAqUnrollF32>, 256, 0));
         d.aq_blocks_per_sm[DSV32_F32] = nb > 0 ? nb : 1;
-        DSV32_CUDA_TRY(
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, act_quant_kernel<__nv_bfloat16, kAqEpl16, kAqUnroll16>,
-                                                          256, 0));
+        DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &nb, act_quant16_kernel<__nv_bfloat16, false, kAqUnroll16>, 256, 0));
         d.aq_blocks_per_sm[DSV32_BF16] = nb > 0 ? nb : 1;
         DSV32_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &nb, act_quant_kernel<__half, kAqEpl16, kAqUnroll16>, 256, 0));
+            &nb, act_quant16_kernel<__half, false, kAqUnroll16>, 256, 0));
         d.aq_blocks_per_sm[DSV32_F16] = nb > 0 ? nb : 1;
       }
       if (!g_encode) {
@@ -672,11 +671,19 @@ int dsv32_act_quant(const void* x, int x_dtype, int64_t rows, int64_t n, int rou
   if (x_dtype == DSV32_F32)
     return launch(act_quant_kernel<float, kAqEplF32, kAqUnrollF32>, g, threads, 0, st, what,
                   static_cast<const float*>(x), y, s, groups, round_scale);
-  if (x_dtype == DSV32_BF16)
-    return launch(act_quant_kernel<__nv_bfloat16, kAqEpl16, kAqUnroll16>, g, threads, 0, st, what,
-                  static_cast<const __nv_bfloat16*>(x), y, s, groups, round_scale);
-  return launch(act_quant_kernel<__half, kAqEpl16, kAqUnroll16>, g, threads, 0, st, what,
-                static_cast<const __half*>(x), y, s, groups, round_scale);
+  const char* what16 = "act_quant16_kernel launch";
+  if (x_dtype == DSV32_BF16) {
+    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+    return round_scale ? launch(act_quant16_kernel<__nv_bfloat16, true, kAqUnroll16>, g, threads, 0, st, what16, xb,
+                                y, s, groups)
+                       : launch(act_quant16_kernel<__nv_bfloat16, false, kAqUnroll16>, g, threads, 0, st, what16,
+                                xb, y, s, groups);
+  }
+  const __half* xh = static_cast<const __half*>(x);
+  return round_scale ? launch(act_quant16_kernel<__half, true, kAqUnroll16>, g, threads, 0, st, what16, xh, y, s,
+                              groups)
+                     : launch(act_quant16_kernel<__half, false, kAqUnroll16>, g, threads, 0, st, what16, xh, y, s,
+                              groups);
 }
 
 int dsv32_int8_gemm(const int8_t* a, const float* a_s, const int8_t* b, const float* b_s, void* c, int c_dtype,

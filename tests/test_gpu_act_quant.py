@@ -120,3 +120,25 @@ def test_act_quant_all_ties_large(rs):
     np.testing.assert_array_equal(npy(s), sr)
     np.testing.assert_array_equal(npy(y), yr)
     assert_no_device_error()
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rs", [False, True])
+def test_act_quant_16bit_ties_and_neighbours(dt, rs):
+    """16-bit inputs whose quotients x / s are exact or near rounding ties: each group's values are
+    amax * (2k + 1) / 254 rounded to the input type, then moved by -1, 0 or +1 unit in the last
+    place, on a multi-wave input with a ragged last iteration (1031 rows)."""
+    g = torch.Generator().manual_seed(21)
+    rows, n = 1031, 4096
+    amax = (torch.rand(rows, n // 128, 1, generator=g) * 8 + 0.01).to(dt).float()
+    k = torch.randint(-127, 127, (rows, n // 128, 128), generator=g).float()
+    x = (amax * (2 * k + 1) / 254).to(dt)
+    nudge = torch.randint(-1, 2, x.shape, generator=g).to(torch.int16)
+    x = (x.view(torch.int16) + nudge).view(dt).float()  # one ulp away in magnitude, sign kept
+    x[..., 0] = amax[..., 0]
+    x = x.to(dt).reshape(rows, n)
+    y, s = D.act_quant(x.to(DEV), rs)
+    yr, sr = O.act_quant_ref(f32_of(x), rs)
+    np.testing.assert_array_equal(npy(s), sr)
+    np.testing.assert_array_equal(npy(y), yr)
+    assert_no_device_error()

@@ -240,6 +240,31 @@ DSV32_DEV float aq_scale_t(float amax) {
   return aq_scale(amax, kRound);
 }
 
+// round_half_even(x / s) for EPL values of one group with scale s (|x| <= the group's amax), returned as
+// the fp32 bits of q + 1.5 * 2^23 (low byte = q as int8), by the branch-free exact path above; a scale
+// that is not finite (an infinity or NaN in the group) takes the IEEE division per value.
+template <int EPL>
+DSV32_DEV void aq_quant_exact(const float (&f)[EPL], float sc, uint32_t (&q)[EPL]) {
+  constexpr float kMagic = 12582912.0f;
+  if (sc < INFINITY) {
+    const float z = __frcp_rn(sc);
+    const float2 z2 = make_float2(z, z), ns2 = make_float2(-sc, -sc), m2 = make_float2(kMagic, kMagic);
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+      const float2 x2 = make_float2(f[e], f[e + 1]);
+      const float2 y = __fmul2_rn(x2, z2);
+      const float2 r = __ffma2_rn(y, ns2, x2);   // x - y * s, exact
+      const float2 qq = __ffma2_rn(r, z2, y);    // RN(x / s)
+      const float2 big = __fadd2_rn(qq, m2);     // rint, ties to even, + 1.5 * 2^23
+      q[e] = __float_as_uint(big.x);
+      q[e + 1] = __float_as_uint(big.y);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) q[e] = __float_as_uint(aq_exact_bits(f[e], sc));
+  }
+}
+
 template <typename T, bool kRound>
 DSV32_DEV void aq16_slot(const uint4& raw, uint2& out, float& sc) {
   float f[8];
@@ -249,25 +274,8 @@ DSV32_DEV void aq16_slot(const uint4& raw, uint2& out, float& sc) {
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
   sc = aq_scale_t<kRound>(max_nan(a, 1e-4f));  // NaN anywhere in the group -> NaN
-  constexpr float kMagic = 12582912.0f;
   uint32_t q[8];
-  if (sc < INFINITY) {
-    const float z = __frcp_rn(sc);
-    const float2 z2 = make_float2(z, z), ns2 = make_float2(-sc, -sc), m2 = make_float2(kMagic, kMagic);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float2 x2 = make_float2(f[e], f[e + 1]);
-      const float2 y = __fmul2_rn(x2, z2);
-      const float2 r = __ffma2_rn(y, ns2, x2);      // x - y * s, exact
-      const float2 qq = __ffma2_rn(r, z2, y);       // RN(x / s)
-      const float2 big = __fadd2_rn(qq, m2);        // rint, ties to even, + 1.5 * 2^23
-      q[e] = __float_as_uint(big.x);
-      q[e + 1] = __float_as_uint(big.y);
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) q[e] = __float_as_uint(aq_exact_bits(f[e], sc));
-  }
+  aq_quant_exact<8>(f, sc, q);
   out = make_uint2(aq_pack4(q[0], q[1], q[2], q[3]), aq_pack4(q[4], q[5], q[6], q[7]));
 }
 

@@ -17,8 +17,9 @@
 //   of W [N, K], s = max(amax, 1e-4) / 127 (an fp32 division), y = clamp(rint(x / s), -127, 127);
 //   scales [N/128, K/128]. One CTA of 512 threads per block; each thread keeps 32 values in registers.
 //
-// Both use act_quant's exact rounding (aq_quant_lane): rint(fl(x / s)) without a per-value
-// division, valid for any scale s with |x / s| <= 127 + tiny.
+// Both use act_quant's branch-free exact rounding (aq_quant_exact): rint(fl(x / s)) from the
+// correctly rounded reciprocal and one exact-remainder correction per value, valid for any normal
+// scale s with |x / s| <= 127 + tiny.
 #pragma once
 #include "act_quant.cuh"
 
@@ -120,10 +121,9 @@ __global__ void __launch_bounds__(kRqThreads, 4) rotate_quant_kernel(const T* __
 #pragma unroll
     for (int o = LPV / 2; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
     const float sc = max_nan(a, 1e-4f) * (1.0f / 127.0f);
-    const float rc = rcp_1ulp(sc);
     if (valid) {
       uint32_t q[16];
-      aq_quant_lane<16>(v, sc, rc, q);
+      aq_quant_exact<16>(v, sc, q);
       __stcs(reinterpret_cast<uint4*>(y + row * 128 + sl * 16), pack16(q));
       // s_mul: the indexer's head weights, which take the per-vector query scale (w * qs,
       // bench_indexer_e2e.py:55: one fp32 rounding, as the reference's product)
@@ -160,11 +160,10 @@ __global__ void __launch_bounds__(kWqThreads, 2) weight_quant_kernel(const T* __
 #pragma unroll
   for (int i = 1; i < kWqThreads / 32; ++i) a = max_nan(a, red[i]);
   const float sc = __fdiv_rn(max_nan(a, 1e-4f), 127.0f);
-  const float rc = rcp_1ulp(sc);
   uint32_t q[16];
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
-    aq_quant_lane<16>(*reinterpret_cast<const float(*)[16]>(v + 16 * j), sc, rc, q);
+    aq_quant_exact<16>(*reinterpret_cast<const float(*)[16]>(v + 16 * j), sc, q);
     *reinterpret_cast<uint4*>(wq + row * k + col + 64 * j) = pack16(q);
   }
   if (tid == 0) ws[nb * kb_count + kb] = sc;

@@ -15,10 +15,10 @@
 // warp handles UNROLL consecutive group-slots per iteration so several 16-byte loads
 // are in flight per lane (HBM latency hiding).
 //
-// Per value the work stays on the FP32 pipe: amax with a NaN-propagating max, the rounding as a
-// fused multiply-add with 1.5 * 2^23 whose result bits carry the int8 (aq_quant_lane), and byte
-// permutes to pack four results; no float -> int conversion instruction. Values within 2^-14 of a
-// rounding tie (about 1 in 8000) are recomputed with the IEEE division.
+// Per value the work stays on the FP32 pipe: amax with a NaN-propagating max, the exact quotient
+// and its rounding by packed f32x2 multiplies, FMAs and adds whose result bits carry the int8
+// (aq_quant_exact), and byte permutes to pack four results; no float -> int conversion and no
+// division per value, no branch.
 #pragma once
 #include "common.cuh"
 
@@ -53,14 +53,6 @@ DSV32_DEV float max_nan(float a, float b) {
   return r;
 }
 
-// Reciprocal with at most 1 ulp of error (the PTX approximate reciprocal): enough for
-// aq_quant_lane, whose exactness argument allows 2^-23 relative error in r.
-DSV32_DEV float rcp_1ulp(float x) {
-  float r;
-  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
 // fp32 scale from the group amax (already floored), both formats.
 DSV32_DEV float aq_scale(float amax, bool round_scale) {
   float s = amax * (1.0f / 127.0f);  // fl32(1/127) times fl32(amax), one fp32 rounding
@@ -76,61 +68,45 @@ DSV32_DEV float aq_scale(float amax, bool round_scale) {
   return s;
 }
 
-constexpr float kAqTieBound = 0.5f - 6.103515625e-05f;  // 1/2 - 2^-14
-
 // fp32 bits of rint(fl(x / s)) + 1.5 * 2^23 through the IEEE division; NaN -> 0.
 DSV32_DEV float aq_exact_bits(float x, float s) {
   const float v = rintf(__fdiv_rn(x, s));
   return (v == v) ? v + 12582912.0f : 12582912.0f;
 }
 
-// round_half_even(x / s) for |x| <= amax, s = amax-derived scale (|x / s| <= 127 + tiny), returned as
-// the fp32 bits of q + 1.5 * 2^23, whose low byte is q as a two's-complement int8. No conversion
-// instruction: fma(x, r, 1.5 * 2^23) rounds the exact product x * r once, to the nearest integer
-// (ties to even, since 1.5 * 2^23 is even and the float spacing there is 1). With r within 1 ulp
-// of 1/s, x * r is within 2^-16 + 2^-18 of fl(x / s) for |q| < 128 (2^-23 relative for r, half an
-// ulp for the quotient), so rint(x * r) == rint(fl(x / s)) unless x * r lies within 2^-14 of a half
-// integer; those (about 1 in 8000) and NaN products take the IEEE division. NaN converts to 0.
-// Applied to the EPL values of one lane with a single (rarely taken) branch: the fast results and one
-// "near a tie / NaN" flag per lane, then the exact path for the flagged values only.
-// Pairs of values use the packed f32x2 FMA: big = x*r + M, -n = big*(-1) + M (exact), t = x*r - n.
-// kSquares selects how the near-tie flag is formed: one packed t * t - c per pair whose sign bits
-// are AND-ed (fewer instructions; [2048, 7168] fp32: 11.6 -> 11.2 us), with c = 1/4 - 2^-14 <
-// bound^2 so that an unflagged value has |t| < bound, and a scale that is not finite (a NaN or
-// infinity in the group) sending the lane to the exact path; or per-value |t| <= bound compares
-// (bf16 input: 11.9 us against 12.1 us for the packed form).
-template <int EPL, bool kSquares = true>
-DSV32_DEV void aq_quant_lane(const float (&f)[EPL], float s, float r, uint32_t (&bits)[EPL]) {
+// round_half_even(x / s) for EPL values of one group with scale s (|x| <= the group's amax), returned as
+// the fp32 bits of q + 1.5 * 2^23 (low byte = q as int8), exactly and without a branch per value:
+// with z = RN(1/s) (the correctly rounded reciprocal, once per group) and y = RN(x * z),
+//   q = RN(y + RN(x - y * s) * z) = RN(x / s)
+// (Markstein's theorem: y is within one ulp of x / s, so the remainder x - y * s is exact in one FMA,
+// and one correction with a correctly rounded reciprocal gives the correctly rounded quotient; valid
+// without overflow or underflow, which |q| <= 127.x and s >= 1e-4 / 127 rule out). RN(q + 1.5 * 2^23)
+// then rounds q to an integer with ties to even; its low byte is the int8. Per pair of values one
+// packed multiply, two packed FMAs and one packed add. A scale that is not finite (an infinity or
+// NaN in the group) takes the IEEE division per value (aq_exact_bits: NaN -> 0).
+template <int EPL>
+DSV32_DEV void aq_quant_exact(const float (&f)[EPL], float sc, uint32_t (&q)[EPL]) {
   constexpr float kMagic = 12582912.0f;
-  const float2 r2 = make_float2(r, r), m2 = make_float2(kMagic, kMagic), neg1 = make_float2(-1.f, -1.f);
-  const float2 c2 = make_float2(-0.24993896484375f, -0.24993896484375f);
-  bool slow = false;
-  uint32_t neg = 0xFFFFFFFFu;
+  if (sc < INFINITY) {
+    const float z = __frcp_rn(sc);
+    const float2 z2 = make_float2(z, z), ns2 = make_float2(-sc, -sc), m2 = make_float2(kMagic, kMagic);
 #pragma unroll
-  for (int e = 0; e < EPL; e += 2) {
-    const float2 x2 = make_float2(f[e], f[e + 1]);
-    const float2 big = __ffma2_rn(x2, r2, m2);
-    const float2 t = __ffma2_rn(x2, r2, __ffma2_rn(big, neg1, m2));
-    if constexpr (kSquares) {
-      const float2 q = __ffma2_rn(t, t, c2);
-      neg &= __float_as_uint(q.x) & __float_as_uint(q.y);
-    } else {
-      slow |= !(fabsf(t.x) <= kAqTieBound) || !(fabsf(t.y) <= kAqTieBound);
+    for (int e = 0; e < EPL; e += 2) {
+      const float2 x2 = make_float2(f[e], f[e + 1]);
+      const float2 y = __fmul2_rn(x2, z2);
+      const float2 r = __ffma2_rn(y, ns2, x2);   // x - y * s, exact
+      const float2 qq = __ffma2_rn(r, z2, y);    // RN(x / s)
+      const float2 big = __fadd2_rn(qq, m2);     // rint, ties to even, + 1.5 * 2^23
+      q[e] = __float_as_uint(big.x);
+      q[e + 1] = __float_as_uint(big.y);
     }
-    bits[e] = __float_as_uint(big.x);
-    bits[e + 1] = __float_as_uint(big.y);
-  }
-  if constexpr (kSquares) slow = !(neg >> 31) || !(s < INFINITY);
-  if (slow) {
+  } else {
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const float t = fmaf(f[e], r, -(__uint_as_float(bits[e]) - kMagic));
-      if (!(fabsf(t) <= kAqTieBound)) bits[e] = __float_as_uint(aq_exact_bits(f[e], s));
-    }
+    for (int e = 0; e < EPL; ++e) q[e] = __float_as_uint(aq_exact_bits(f[e], sc));
   }
 }
 
-// Low bytes of four aq_quant_lane results, in order, as one 32-bit word.
+// Low bytes of four quantised results (aq_quant_exact bits), in order, as one 32-bit word.
 DSV32_DEV uint32_t aq_pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
@@ -189,10 +165,9 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
       for (int o = LPG / 2; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
       const float amax = max_nan(a, 1e-4f);  // NaN anywhere in the group -> NaN
       const float sc = aq_scale(amax, round_scale != 0);
-      const float rc = rcp_1ulp(sc);
       if (valid) {
         uint32_t qb[EPL];
-        aq_quant_lane<EPL, sizeof(T) == 4>(f, sc, rc, qb);
+        aq_quant_exact<EPL>(f, sc, qb);
         int8_t* dst = y + g * 128 + sl * EPL;
         if constexpr (EPL == 4) {
           __stcs(reinterpret_cast<unsigned int*>(dst), aq_pack4(qb[0], qb[1], qb[2], qb[3]));
@@ -219,50 +194,17 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
 namespace dsv32 {
 
 // ---------------------------------------------------------------- 16-bit input (bf16 / fp16)
-// Same results as act_quant_kernel, computed without the near-tie test. 16-bit inputs are full of
-// exact and near rounding ties (a value equal to amax / 2 gives x / s = 63.5 up to the rounding of s:
-// about a third of the groups of normal bf16 data hold one), so the fast-path-plus-fix-up form ran
-// its exact path in most warp iterations. Here every value takes one exact path with no branch:
-// with z = RN(1/s) (the correctly rounded reciprocal, once per group) and y = RN(x * z),
-//   q = RN(y + RN(x - y * s) * z) = RN(x / s)
-// (Markstein's theorem: y is within one ulp of x / s, so the remainder x - y * s is exact in one
-// FMA, and one correction with a correctly rounded reciprocal gives the correctly rounded
-// quotient; valid without overflow or underflow, which |q| <= 127.x and s >= 1e-4 / 127 rule out).
-// Then RN(q + 1.5 * 2^23) rounds q to an integer, ties to even, and its low byte is the int8.
-// Per pair of values: one packed multiply, two packed FMAs, one packed add. A group holding an
-// infinity or NaN (scale not finite) takes the IEEE division per value (aq_exact_bits: NaN -> 0).
-// Layout: one 128-value group per 16 lanes (8 values per lane, one 16-byte load), two groups per
-// warp slot, UNROLL consecutive slots per warp iteration; iterations whose slots are all complete
-// run without validity tests, their loads and stores at constant offsets from one base pointer.
+// 16-bit input moves 60 % of fp32's bytes for the same work per value, so its kernel is leaner:
+// one 128-value group per 16 lanes (8 values per lane, one 16-byte load), two groups per warp slot,
+// UNROLL consecutive slots per warp iteration; the scale format is a template parameter; iterations
+// whose slots are all complete run without validity tests, their loads and stores at constant
+// offsets from one base pointer. (16-bit data is full of rounding ties: a value equal to amax / 2
+// gives x / s = 63.5 up to the rounding of s, and about a third of the groups of normal bf16 data
+// hold one, which is why the exact rounding has no near-tie test and fix-up branch.)
 
 template <bool kRound>
 DSV32_DEV float aq_scale_t(float amax) {
   return aq_scale(amax, kRound);
-}
-
-// round_half_even(x / s) for EPL values of one group with scale s (|x| <= the group's amax), returned as
-// the fp32 bits of q + 1.5 * 2^23 (low byte = q as int8), by the branch-free exact path above; a scale
-// that is not finite (an infinity or NaN in the group) takes the IEEE division per value.
-template <int EPL>
-DSV32_DEV void aq_quant_exact(const float (&f)[EPL], float sc, uint32_t (&q)[EPL]) {
-  constexpr float kMagic = 12582912.0f;
-  if (sc < INFINITY) {
-    const float z = __frcp_rn(sc);
-    const float2 z2 = make_float2(z, z), ns2 = make_float2(-sc, -sc), m2 = make_float2(kMagic, kMagic);
-#pragma unroll
-    for (int e = 0; e < EPL; e += 2) {
-      const float2 x2 = make_float2(f[e], f[e + 1]);
-      const float2 y = __fmul2_rn(x2, z2);
-      const float2 r = __ffma2_rn(y, ns2, x2);   // x - y * s, exact
-      const float2 qq = __ffma2_rn(r, z2, y);    // RN(x / s)
-      const float2 big = __fadd2_rn(qq, m2);     // rint, ties to even, + 1.5 * 2^23
-      q[e] = __float_as_uint(big.x);
-      q[e + 1] = __float_as_uint(big.y);
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) q[e] = __float_as_uint(aq_exact_bits(f[e], sc));
-  }
 }
 
 template <typename T, bool kRound>

@@ -7,8 +7,8 @@ Default workload: block-scaled int8_gemm "expert up", M=40
 bf16 out, per GPU. With N GPUs (torchrun, one rank per GPU) the weight is sharded by N: global
 N = 2048 * world, each rank computes its own 2048 columns (weak scaling, no data-path collective).
 The default line also carries a `secondary` list measured the same way: at one GPU the rest of
-BASELINE's metric (indexer prefill step 4096^2 causal with top-2048, act_quant fp32 and bf16) and
-the long-context indexer; at N GPUs the long-context indexer (4096 queries x 131072 keys, keys
+BASELINE's metric (indexer prefill step 4096^2 causal with top-2048, act_quant fp32 and bf16), the
+long-context indexer and the decode cases (expert-down GEMM at M=32, indexer 4 x 32768); at N GPUs the long-context indexer (4096 queries x 131072 keys, keys
 sharded by range over the ranks, strong scaling) with its per-stage times and a parity check of the
 merged selection against a one-GPU selection over all keys.
 Other workloads (--workload): gemm_down (K=2048 N=7168, --m), act_quant (--aq-dtype), index_prefill,
@@ -281,6 +281,13 @@ class GemmWorkload(Workload):
         return (self.D.int8_gemm(A, a_s, B, b_s, out_dtype=self.odt),)
 
     def roofline(self, kernel_ms, peaks, src, traffic):
+        if self.M <= 64:  # decode-sized: the weights stream once, HBM bounds the launch
+            peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+            ach = self.bytes_alg / (kernel_ms * 1e-3) / 1e9
+            return {"bound": "hbm", "achieved": round(ach, 1), "peak": round(peak, 1), "unit": "GB/s",
+                    "frac": round(ach / peak, 4), "traffic": traffic.get(f"int8_gemm_{self.name}"),
+                    "peak_note": f"{src} STREAM-style copy; {self.ops / (kernel_ms * 1e-3) / 1e12:.1f} TOP/s",
+                    "algorithmic_bytes": self.bytes_alg, "ops_per_launch": self.ops}
         peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
         ach = self.ops / (kernel_ms * 1e-3) / 1e12
         return {"bound": "tensor", "achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TOP/s",
@@ -741,6 +748,8 @@ def make_workload(name, args, rank, world):
         return GemmWorkload(4096, 2048, 7168, "bf16", rank, world, "expert_up")
     if name == "gemm_down":
         return GemmWorkload(args.m, 7168, 2048, args.out, rank, world, f"expert_down_m{args.m}", seed=1)
+    if name == "gemm_down_m32":  # BASELINE's latency headline of the expert-down sweep, bf16 out
+        return GemmWorkload(32, 7168, 2048, "bf16", rank, world, "expert_down_m32", seed=1)
     if name == "act_quant":
         return ActQuantWorkload(2048, 7168, args.aq_dtype, rank, world)
     if name in ("act_quant_fp32", "act_quant_bf16"):
@@ -758,11 +767,12 @@ def make_workload(name, args, rank, world):
 
 def secondary_names(args, world):
     """The rest of BASELINE's metric beside the headline GEMM: at one GPU the indexer prefill step,
-    act_quant fp32 / bf16 and the long-context indexer; at N GPUs the key-sharded long indexer."""
+    act_quant fp32 / bf16, the long-context indexer and the decode cases (expert-down GEMM at M=32,
+    the indexer over 4 queries x 32768 keys); at N GPUs the key-sharded long indexer."""
     if args.workload != "gemm_up" or args.no_secondary:
         return []
     if world == 1:
-        return ["index_prefill", "act_quant_fp32", "act_quant_bf16", "index_long"]
+        return ["index_prefill", "act_quant_fp32", "act_quant_bf16", "index_long", "gemm_down_m32", "index_decode"]
     return ["index_long"]
 
 

@@ -566,10 +566,9 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
       if (int rc = topk_reg_launch(cv, rb, cap, cap, ci, cap, 0, kk, out_idx + r0 * k, out_val + r0 * k, 0, 0, 0, cap,
                                    1, st, RowParts{}, cn))
         return rc;
-      const int64_t fb_grid = std::min<int64_t>(rb, 2 * static_cast<int64_t>(info->num_sms));
-      if (int rc = launch(topk_gmem_kernel<1024>, static_cast<unsigned>(fb_grid), 1024, 0, st, "topk kernel launch",
+      if (int rc = launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rb), 1024, 0, st, "topk kernel launch",
                           scores + r0 * ld, ld, nn, cin, cand_ld, idx_offset, kk, out_idx + r0 * k, out_val + r0 * k,
-                          cm, cs, static_cast<long long>(r0), static_cast<const int*>(cn), static_cast<long long>(rb)))
+                          cm, cs, static_cast<long long>(r0), static_cast<const int*>(cn)))
         return rc;
     }
     return DSV32_OK;
@@ -620,7 +619,7 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   }
   return launch(topk_gmem_kernel<1024>, static_cast<unsigned>(rows), 1024, 0, st, "topk kernel launch", scores, ld, nn,
                 cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, static_cast<long long>(causal_start), 0LL,
-                static_cast<const int*>(nullptr), static_cast<long long>(rows));
+                static_cast<const int*>(nullptr));
 }
 
 }  // namespace

@@ -523,9 +523,6 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
 // ---------------------------------------------------------------------------- long rows
 // Positions at or past the row's visible length (causal rows) are -inf without being read. With
 // row_state, only rows whose state is kRowFallback are selected (the others finished elsewhere).
-// CTA c handles rows c, c + gridDim.x, ... of the nrows: one CTA per row for plain rows, a grid of
-// a few CTAs per SM after the filter, where almost every row is already done (4096 CTAs that only
-// read their row's state took 11 us).
 constexpr int kRowFallback = -2;
 template <int THREADS>
 __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restrict__ vals, long long ld, int n,
@@ -533,15 +530,14 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
                                                             long long idx_offset, int k, int32_t* __restrict__ out_idx,
                                                             float* __restrict__ out_val, int causal_m,
                                                             long long causal_start, long long causal_row0,
-                                                            const int* __restrict__ row_state, long long nrows) {
+                                                            const int* __restrict__ row_state) {
   __shared__ SelShared sh;
   int parity = 0;
+  const long long row = blockIdx.x;
+  const float* v = vals + row * ld;
   pdl_wait();
   pdl_launch_dependents();
-  for (long long row = blockIdx.x; row < nrows; row += gridDim.x) {
-  if (row_state && row_state[row] != kRowFallback) continue;  // (block-uniform)
-  __syncthreads();  // the previous row's reads of shared memory are done
-  const float* v = vals + row * ld;
+  if (row_state && row_state[row] != kRowFallback) return;
   const int valid = row_valid(row + causal_row0, n, causal_m, causal_start);
   auto key_at = [&](int i) { return i < valid ? fkey(__ldg(v + i)) : kNegInfKey; };
   int n_above = 0;
@@ -613,7 +609,6 @@ __global__ void __launch_bounds__(THREADS) topk_gmem_kernel(const float* __restr
       ov[o] = x;
       ++o;
     }
-  }
   }
 }
 

@@ -46,6 +46,8 @@ SIGNATURES = {
     "dsv32_last_error_message": (ctypes.c_char_p, []),
     "dsv32_topk_parts": (_i32, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _i64, _i64, _i64, _i64, _p, _p, _p,
                                 _i64, _p]),
+    "dsv32_topk_parts_to": (_i32, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _i64, _i64, _i64, _i64,
+                                   ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _p, _i64, _p]),
     "dsv32_device_alloc": (_i32, [_i64, ctypes.POINTER(_p)]),
     "dsv32_device_free": (_i32, [_p]),
     "dsv32_ipc_export": (_i32, [_p, _p]),
@@ -54,7 +56,7 @@ SIGNATURES = {
     "dsv32_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 IPC_HANDLE_BYTES = 64
 
 _LIB = None

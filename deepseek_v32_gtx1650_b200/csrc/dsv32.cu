@@ -523,9 +523,23 @@ int64_t topk_ws_bytes(int64_t rows, int64_t n, int64_t k, int nparts) {
 int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const int32_t* cand_idx, int64_t cand_ld,
               int64_t idx_offset, int64_t k, int32_t* out_idx, float* out_val, void* workspace, int64_t ws_bytes,
               void* stream, int64_t causal_m = 0, int64_t causal_start = 0,
-              const dsv32::topk::RowParts* parts = nullptr) {
+              const dsv32::topk::RowParts* parts = nullptr, const dsv32::topk::RowParts* dests = nullptr) {
   const dsv32::topk::RowParts no_parts{};
   const dsv32::topk::RowParts& p0 = parts ? *parts : no_parts;  // addressing of the first pass
+  // dests (ndst > 0): the final pass writes each row to every destination pair instead of out_idx /
+  // out_val (which then only has to be non-null); intermediate passes write the workspace as usual.
+  // Destinations of row batch r0: the final addressing with out_idx / out_val of dests offset by r0 rows.
+  auto final_parts = [&](const dsv32::topk::RowParts& base, int64_t r0) {
+    dsv32::topk::RowParts f = base;
+    if (dests) {
+      f.ndst = dests->ndst;
+      for (int d = 0; d < dests->ndst; ++d) {
+        f.out_idx[d] = dests->out_idx[d] + r0 * k;
+        f.out_val[d] = dests->out_val[d] + r0 * k;
+      }
+    }
+    return f;
+  };
   if ((!scores && !parts) || !out_idx || !out_val) return DSV32_ERR_INVALID_ARG;
   if (rows < 1 || n < 1 || k < 1 || k > n || (!parts && ld < n)) return DSV32_ERR_INVALID_ARG;
   if (cand_idx && cand_ld < n) return DSV32_ERR_INVALID_ARG;
@@ -540,7 +554,7 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
   const int cm = causal_m > 0 && causal_m <= 0x7FFFFFFFLL ? static_cast<int>(causal_m) : 0;
   if (n <= kTopkRegMax) {
     return topk_reg_launch(scores, rows, nn, ld, cand_idx, cand_ld, idx_offset, kk, out_idx, out_val, cm, causal_start,
-                           0, nn, 1, st, p0);
+                           0, nn, 1, st, final_parts(p0, 0));
   }
   if (!parts && workspace && filter_shape(n, k) && rows >= info->num_sms &&
       ws_bytes >= filter_per_row(kk)) {
@@ -614,7 +628,8 @@ int topk_impl(const float* scores, int64_t rows, int64_t n, int64_t ld, const in
         in_cs = 0;
       }
       if (int rc = topk_reg_launch(in_v, rb, plan.n[stages], in_ld, in_c, in_cld, off, kk, out_idx + r0 * k,
-                                   out_val + r0 * k, in_cm, in_cs, r0, plan.n[stages], 1, st))
+                                   out_val + r0 * k, in_cm, in_cs, r0, plan.n[stages], 1, st,
+                                   final_parts(no_parts, r0)))
         return rc;
     }
     return DSV32_OK;
@@ -820,6 +835,33 @@ int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_i
   parts.n = nparts;
   return topk_impl(nullptr, rows, nparts * part_len, part_ld, nullptr, 0, 0, k, out_idx, out_val, workspace,
                    workspace_bytes, stream, 0, 0, &parts);
+}
+
+int dsv32_topk_parts_to(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
+                        int64_t part_ld, int64_t part_len, int64_t k, int32_t* const* out_idx, float* const* out_val,
+                        int ndst, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!part_vals || !part_ids || nparts < 1 || nparts > dsv32::topk::kMaxParts) return DSV32_ERR_INVALID_ARG;
+  if (!out_idx || !out_val || ndst < 1 || ndst > dsv32::topk::kMaxParts) return DSV32_ERR_INVALID_ARG;
+  if (rows < 1 || part_len < 1 || part_ld < part_len || k < 1 || k > nparts * part_len) return DSV32_ERR_INVALID_ARG;
+  if (part_len % 16 != 0 || nparts * part_len > (1LL << 30)) return DSV32_ERR_UNSUPPORTED;
+  if (k > dsv32::topk::kStageMax) return DSV32_ERR_UNSUPPORTED;  // rows are staged once, copied per destination
+  dsv32::topk::RowParts parts{}, dests{};
+  for (int j = 0; j < nparts; ++j) {
+    if (!part_vals[j] || !part_ids[j]) return DSV32_ERR_INVALID_ARG;
+    parts.v[j] = part_vals[j];
+    parts.id[j] = part_ids[j];
+  }
+  for (int d = 0; d < ndst; ++d) {
+    if (!out_idx[d] || !out_val[d]) return DSV32_ERR_INVALID_ARG;
+    dests.out_idx[d] = out_idx[d];
+    dests.out_val[d] = out_val[d];
+  }
+  parts.ld = part_ld;
+  parts.len = static_cast<int>(part_len);
+  parts.n = nparts;
+  dests.ndst = ndst;
+  return topk_impl(nullptr, rows, nparts * part_len, part_ld, nullptr, 0, 0, k, out_idx[0], out_val[0], workspace,
+                   workspace_bytes, stream, 0, 0, &parts, &dests);
 }
 
 int dsv32_int8_index_topk(const int8_t* q, const float* w, const int8_t* k, const float* k_s, float* scores,

@@ -227,11 +227,17 @@ DSV32_DEV void copy_out_staged(const int32_t* sidx, const float* sval, int32_t* 
 // its candidate ids at id[j] + r * ld): the per-rank top-k lists of a key-sharded selection, read in
 // place, possibly from other GPUs' memory. n == 0: rows are plain (vals / cand_idx addressing).
 constexpr int kMaxParts = 16;
+// ndst > 0: the selected row is written to each of ndst output pairs (out_idx[d], out_val[d], row-major
+// [rows, k] like out_idx / out_val) instead of out_idx / out_val: a merged row block lands in every
+// rank's output buffer (local or mapped from other GPUs) in one pass. Requires k <= kStageMax (the
+// row is staged in shared memory and copied out once per destination).
 struct RowParts {
   const float* v[kMaxParts];
   const int32_t* id[kMaxParts];
+  int32_t* out_idx[kMaxParts];
+  float* out_val[kMaxParts];
   long long ld;
-  int len, n;
+  int len, n, ndst;
 };
 
 // Positions past n hold key 0 (below every real key): they never count as above -inf, never reach a
@@ -304,23 +310,26 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   //    first k positions: no key ranks below the masked -inf tail, and the tail's ties go to the
   //    lowest positions. Output j is position j, copied straight to the outputs.
   if (valid <= k) {
-    int32_t* oi = out_idx + out_row * k;
-    float* ov = out_val + out_row * k;
-    if (parts.n > 0) {
-      for (int j = tid; j < k; j += THREADS) {
-        const int pj = (seg0 + j) / parts.len;
-        const long long off = row * parts.ld + (seg0 + j - pj * parts.len);
-        oi[j] = parts.id[pj][off];
-        ov[j] = j < valid ? __ldg(parts.v[pj] + off) : -INFINITY;
-      }
-    } else {
-      const float* v = vals + row * ld + seg0;
-      const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
-      for (int j = tid; j < k; j += THREADS) {
-        oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
-        ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
+    for (int d = 0; d < max(parts.ndst, 1); ++d) {
+      int32_t* oi = (parts.ndst > 0 ? parts.out_idx[d] : out_idx) + out_row * k;
+      float* ov = (parts.ndst > 0 ? parts.out_val[d] : out_val) + out_row * k;
+      if (parts.n > 0) {
+        for (int j = tid; j < k; j += THREADS) {
+          const int pj = (seg0 + j) / parts.len;
+          const long long off = row * parts.ld + (seg0 + j - pj * parts.len);
+          oi[j] = parts.id[pj][off];
+          ov[j] = j < valid ? __ldg(parts.v[pj] + off) : -INFINITY;
+        }
+      } else {
+        const float* v = vals + row * ld + seg0;
+        const int32_t* cand_row = cand_idx ? cand_idx + row * cand_ld + seg0 : nullptr;
+        for (int j = tid; j < k; j += THREADS) {
+          oi[j] = cand_row ? cand_row[j] : static_cast<int32_t>(j + seg0 + idx_offset);
+          ov[j] = j < valid ? __ldg(v + j) : -INFINITY;
+        }
       }
     }
+    if (parts.ndst > 0) __threadfence_system();
     return;
   }
   for (int i = tid; i < kRegBins; i += THREADS) sh.u.hist[i] = 0;  // first radix pass
@@ -516,7 +525,14 @@ __global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3) topk_reg_kern
   }
   if (staged) {
     __syncthreads();
-    copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
+    if (parts.ndst > 0) {
+      for (int d = 0; d < parts.ndst; ++d)
+        copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, parts.out_idx[d] + out_row * k,
+                                 parts.out_val[d] + out_row * k, k);
+      __threadfence_system();  // the other GPUs' copies are complete before this CTA exits
+    } else {
+      copy_out_staged<THREADS>(sh.u.out.idx, sh.u.out.val, oi, ov, k);
+    }
   }
 }
 

@@ -224,6 +224,25 @@ def topk_parts_raw(val_ptrs, id_ptrs, rows: int, part_ld: int, part_len: int, k:
     return idx, vals
 
 
+def topk_parts_to_raw(val_ptrs, id_ptrs, rows: int, part_ld: int, part_len: int, k: int, out_idx_ptrs,
+                      out_val_ptrs, device: torch.device, workspace=None):
+    """topk_parts_raw writing every selected row to each (out_idx_ptrs[d], out_val_ptrs[d]) pair of raw
+    [rows, k] device addresses (this GPU's or other GPUs' memory mapped with CUDA IPC) instead of
+    returning it. The writes to other GPUs are complete when the kernel is; order them before the
+    owners read (a collective)."""
+    assert len(out_idx_ptrs) == len(out_val_ptrs) and 1 <= len(out_idx_ptrs) <= 16
+    pv, keep_v = _ptr_array(val_ptrs)
+    pi, keep_i = _ptr_array(id_ptrs)
+    po, keep_o = _ptr_array(out_idx_ptrs)
+    pw, keep_w = _ptr_array(out_val_ptrs)
+    with torch.cuda.device(device):
+        st = torch.cuda.current_stream(device).cuda_stream
+        ws, wsb = workspace if workspace is not None else _topk_workspace(device, st, rows, len(val_ptrs) * part_len,
+                                                                           k, len(val_ptrs))
+        _lib.check(_lib.load().dsv32_topk_parts_to(pv, pi, len(val_ptrs), rows, part_ld, part_len, k, po, pw,
+                                                   len(out_idx_ptrs), ws, wsb, st), "topk_parts_to")
+
+
 def select_topk_parts(vals_list, idx_list, k: int):
     """Top-k of rows given as lists: row r of the concatenation of vals_list[j][r] (each [rows, L]
     fp32, L % 16 == 0) with candidate ids idx_list[j][r] (int32). The lists are read in place (no

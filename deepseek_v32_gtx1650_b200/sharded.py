@@ -10,8 +10,9 @@ Only the two paths that shard naturally are partitioned:
   local top-k (global key ids = lo + position). The lists are then merged by query row: each
   rank's selection lands in a buffer every rank maps with CUDA IPC (PeerLists), a one-element
   all-reduce orders all selections before any read, rank r merges its rows / world rows with the
-  top-k kernel reading every rank's lists in place over NVLink (dsv32_topk_parts), and an
-  all-gather of the merged rows gives every rank the whole result. When the rows do not split
+  top-k kernel reading every rank's lists in place over NVLink and writing the merged rows into every
+  rank's output buffer (dsv32_topk_parts_to), and a second one-element all-reduce orders every merge
+  before any rank reads its output. When the rows do not split
   evenly or peer mappings are unavailable, merge_candidates does the exchange with NCCL
   all-to-alls (or an all-gather). Local lists are position-ordered and concatenated in rank order,
   so ties resolve to the lowest global key id exactly as in the single-GPU selection; the merged
@@ -100,14 +101,30 @@ def merge_candidates(idx: torch.Tensor, vals: torch.Tensor, topk: int, group=Non
     return out_i, out_b.view(torch.float32)
 
 
+class _RawCuda:
+    """A device buffer this process does not own by torch (a dsv32_device_alloc allocation), described
+    by the CUDA array interface so that torch.as_tensor views it without a copy."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+def _raw_view(ptr: int, shape, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    typestr = {torch.int32: "<i4", torch.float32: "<f4"}[dtype]
+    with torch.cuda.device(device):
+        return torch.as_tensor(_RawCuda(ptr, shape, typestr), device=device)
+
+
 class PeerLists:
-    """This rank's top-k lists of `rows` rows (ids [rows, k] int32, then values [rows, k] fp32, in one
-    cudaMalloc allocation) and every peer's, mapped into this process with CUDA IPC, so the merge
-    kernel reads the other ranks' lists in place over NVLink. Built once per (rows, k, device, group)
-    by a collective (all ranks construct it together); released at exit. The merge's top-k workspace
-    (rows of world * k candidates longer than one register pass are selected in stages) is reserved
-    here too, so a merge allocates nothing. `usable` is False on every rank if any rank could not
-    allocate, export or map (the caller then exchanges through NCCL)."""
+    """This rank's top-k lists of `rows` rows (ids [rows, k] int32, then values [rows, k] fp32) and its
+    output rows (ids, then values, [rows, k] each), in one cudaMalloc allocation, and every peer's,
+    mapped into this process with CUDA IPC: the merge kernel reads the other ranks' lists in place
+    over NVLink and writes its merged row block into every rank's output rows. Built once per (rows,
+    k, device, group) by a collective (all ranks construct it together); released at exit. The
+    merge's top-k workspace (rows of world * k candidates longer than one register pass are selected
+    in stages) is reserved here too, so a merge allocates nothing. `usable` is False on every rank if
+    any rank could not allocate, export or map (the caller then exchanges through NCCL)."""
 
     _cache: dict = {}
 
@@ -127,7 +144,7 @@ class PeerLists:
                     ok = False
             base = ctypes.c_void_p()
             handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
-            if ok and lib.dsv32_device_alloc(rows * k * 8, ctypes.byref(base)) == _lib.DSV32_OK:
+            if ok and lib.dsv32_device_alloc(rows * k * 16, ctypes.byref(base)) == _lib.DSV32_OK:
                 self.own = base.value
                 ok = lib.dsv32_ipc_export(base, handle) == _lib.DSV32_OK
             else:
@@ -152,6 +169,9 @@ class PeerLists:
             self.usable = bool(t.item())
         if not self.usable:
             self.close()
+        else:  # this rank's output rows as tensors (copied out after every merge)
+            self.out_ids = _raw_view(self.out_ids_ptr(self.rank), (rows, k), torch.int32, device)
+            self.out_vals = _raw_view(self.out_vals_ptr(self.rank), (rows, k), torch.float32, device)
         self.flag = torch.zeros(1, dtype=torch.int32, device=device)
         atexit.register(self.close)
 
@@ -161,8 +181,15 @@ class PeerLists:
     def vals_ptr(self, r: int, row0: int = 0) -> int:
         return self.bases[r] + 4 * (self.rows + row0) * self.k
 
+    def out_ids_ptr(self, r: int, row0: int = 0) -> int:
+        return self.bases[r] + 4 * (2 * self.rows + row0) * self.k
+
+    def out_vals_ptr(self, r: int, row0: int = 0) -> int:
+        return self.bases[r] + 4 * (3 * self.rows + row0) * self.k
+
     def close(self):
         lib = _lib.load()
+        self.out_ids = self.out_vals = None
         for p in self.opened:
             lib.dsv32_ipc_close(ctypes.c_void_p(p))
         self.opened = []
@@ -218,8 +245,10 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
         _mark(events, "nccl_exchange+merge")
         return midx.view(B, M, topk), mval.view(B, M, topk)
     # Peer-memory exchange: the local selection writes straight into this rank's mapped buffer, a
-    # one-element all-reduce orders every rank's selection before any read, and the merge kernel
-    # reads this rank's row block of every rank's lists in place over NVLink.
+    # one-element all-reduce orders every rank's selection before any read, the merge kernel reads
+    # this rank's row block of every rank's lists in place over NVLink and writes the merged block
+    # into every rank's output rows (plain stores to peer memory, no staging copy), and a second
+    # all-reduce orders every rank's merge before any rank reads its output.
     K.int8_index_topk_into(q, w, k_local, k_s_local, ex.ids_ptr(ex.rank), ex.vals_ptr(ex.rank), topk=topk,
                            causal=causal, start=lstart, key_offset=key_lo)
     _mark(events, "index+local_topk")
@@ -227,17 +256,18 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     _mark(events, "order_allreduce")
     r = rows // world
     r0 = ex.rank * r
-    mi, mv = K.topk_parts_raw([ex.vals_ptr(j, r0) for j in range(world)], [ex.ids_ptr(j, r0) for j in range(world)],
-                              r, topk, topk, topk, q.device, workspace=ex.ws_arg)
-    _mark(events, "merge_peer_lists")
-    # Merged row blocks to every rank. A rank passes this point only after every rank's merge kernel
-    # has run (they precede the all-gather on each stream), so the next call may overwrite the lists.
-    out_i = torch.empty(rows, topk, dtype=torch.int32, device=q.device)
-    out_b = torch.empty(rows, topk, dtype=torch.int32, device=q.device)
-    dist.all_gather_into_tensor(out_i, mi, group=group)
-    dist.all_gather_into_tensor(out_b, mv.view(torch.int32), group=group)
-    _mark(events, "allgather_rows")
-    return out_i.view(B, M, topk), out_b.view(torch.float32).view(B, M, topk)
+    K.topk_parts_to_raw([ex.vals_ptr(j, r0) for j in range(world)], [ex.ids_ptr(j, r0) for j in range(world)],
+                        r, topk, topk, topk, [ex.out_ids_ptr(j, r0) for j in range(world)],
+                        [ex.out_vals_ptr(j, r0) for j in range(world)], q.device, workspace=ex.ws_arg)
+    _mark(events, "merge_to_every_rank")
+    # A rank passes this all-reduce only after every rank's merge kernel has run, so its output rows
+    # are complete, and the next call may overwrite the lists (the next merge writes the outputs only
+    # after the next ordering all-reduce, which follows this rank's copy below).
+    dist.all_reduce(ex.flag, group=group)
+    out_i = ex.out_ids.clone()
+    out_v = ex.out_vals.clone()
+    _mark(events, "done_allreduce+copy")
+    return out_i.view(B, M, topk), out_v.view(B, M, topk)
 
 
 def sharded_int8_gemm(a, a_s, b_local, b_s_local, out_dtype=torch.float32):

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define DSV32_ABI_VERSION 6
+#define DSV32_ABI_VERSION 7
 
 /* Status codes. */
 #define DSV32_OK 0
@@ -195,6 +195,16 @@ int dsv32_weight_quant(const void* w, int w_dtype, int64_t n, int64_t k, int8_t*
 int dsv32_topk_parts(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
                      int64_t part_ld, int64_t part_len, int64_t k, int32_t* out_idx, float* out_val, void* workspace,
                      int64_t workspace_bytes, void* stream);
+
+/* dsv32_topk_parts writing each selected row to ndst output pairs (out_idx[d], out_val[d], each
+ * [rows, k]) instead of one: a rank's merged row block goes straight into every rank's output buffer
+ * (local, or mapped from another GPU with dsv32_ipc_open) in one pass, in place of all-gathering the
+ * merged blocks (same role as dsv32_topk_parts; no reference counterpart). 1 <= ndst <= 16,
+ * k <= 2048. The writes to other GPUs are complete when the kernel is; the caller orders them
+ * before any rank reads its output (a collective after the call). */
+int dsv32_topk_parts_to(const float* const* part_vals, const int32_t* const* part_ids, int nparts, int64_t rows,
+                        int64_t part_ld, int64_t part_len, int64_t k, int32_t* const* out_idx, float* const* out_val,
+                        int ndst, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Device memory another process on the node can map: cudaMalloc on the current device (the pointer
  * is the base of its allocation, as IPC export requires), and its release. */

@@ -38,7 +38,7 @@ def test_library_builds_and_exports_every_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.dsv32_abi_version() == 6
+    assert lib.dsv32_abi_version() == 7
     for code in range(6):
         assert lib.dsv32_status_string(code)
     assert lib.dsv32_status_string(_lib.DSV32_ERR_DEVICE_TIMEOUT).decode().startswith("kernel timed out")
@@ -94,6 +94,14 @@ def test_topk_parts_and_ipc_validation_without_gpu():
     assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 64, 129, fake, fake, *z) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_topk_parts(parts, parts, 2, 4, 64, 40, 8, fake, fake, *z) == _lib.DSV32_ERR_UNSUPPORTED
     assert lib.dsv32_topk_parts(parts, parts, 2, 4, 32, 64, 8, fake, fake, *z) == _lib.DSV32_ERR_INVALID_ARG
+    # the multi-destination form: no destinations, too many, a null destination, k beyond one staged row
+    outs = ctypes.cast((ctypes.c_void_p * 2)(4096, 8192), P)
+    nulls = ctypes.cast((ctypes.c_void_p * 2)(4096, None), P)
+    assert lib.dsv32_topk_parts_to(parts, parts, 2, 4, 64, 64, 8, outs, outs, 0, *z) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts_to(parts, parts, 2, 4, 64, 64, 8, outs, outs, 17, *z) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts_to(parts, parts, 2, 4, 64, 64, 8, nulls, outs, 2, *z) == _lib.DSV32_ERR_INVALID_ARG
+    assert lib.dsv32_topk_parts_to(parts, parts, 2, 4, 4096, 4096, 4096, outs, outs, 2, *z) == \
+        _lib.DSV32_ERR_UNSUPPORTED
     # null arguments of the memory / IPC helpers
     assert lib.dsv32_device_alloc(0, ctypes.byref(ctypes.c_void_p())) == _lib.DSV32_ERR_INVALID_ARG
     assert lib.dsv32_ipc_export(None, fake) == _lib.DSV32_ERR_INVALID_ARG

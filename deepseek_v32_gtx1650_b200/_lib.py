@@ -50,6 +50,7 @@ SIGNATURES = {
                                    ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _p, _i64, _p]),
     "dsv32_device_alloc": (_i32, [_i64, ctypes.POINTER(_p)]),
     "dsv32_device_free": (_i32, [_p]),
+    "dsv32_copy_async": (_i32, [_p, _p, _i64, _p]),
     "dsv32_ipc_export": (_i32, [_p, _p]),
     "dsv32_ipc_open": (_i32, [_p, ctypes.POINTER(_p)]),
     "dsv32_ipc_close": (_i32, [_p]),

@@ -787,6 +787,14 @@ int dsv32_device_alloc(int64_t bytes, void** ptr) {
   return e == cudaSuccess ? DSV32_OK : cuda_fail(e, "cudaMalloc");
 }
 
+int dsv32_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (!dst || !src || bytes < 0) return DSV32_ERR_INVALID_ARG;
+  if (bytes == 0) return DSV32_OK;
+  const cudaError_t e =
+      cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? DSV32_OK : cuda_fail(e, "cudaMemcpyAsync");
+}
+
 int dsv32_device_free(void* ptr) {
   if (!ptr) return DSV32_OK;
   const cudaError_t e = cudaFree(ptr);

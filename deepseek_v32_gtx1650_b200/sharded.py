@@ -9,10 +9,10 @@ Only the two paths that shard naturally are partitioned:
   It scores every query against its keys with the causal limit shifted by -lo and selects its
   local top-k (global key ids = lo + position). The lists are then merged by query row: each
   rank's selection lands in a buffer every rank maps with CUDA IPC (PeerLists), a one-element
-  all-reduce orders all selections before any read, rank r merges its rows / world rows with the
-  top-k kernel reading every rank's lists in place over NVLink and writing the merged rows into every
-  rank's output buffer (dsv32_topk_parts_to), and a second one-element all-reduce orders every merge
-  before any rank reads its output. When the rows do not split
+  all-reduce orders all selections before any read, rank r pulls the other ranks' lists of its rows /
+  world rows into its own memory with the copy engines and merges them with the top-k kernel, which
+  writes the merged rows into every rank's output buffer (dsv32_topk_parts_to), and a second
+  one-element all-reduce orders every merge before any rank reads its output. When the rows do not split
   evenly or peer mappings are unavailable, merge_candidates does the exchange with NCCL
   all-to-alls (or an all-gather). Local lists are position-ordered and concatenated in rank order,
   so ties resolve to the lowest global key id exactly as in the single-GPU selection; the merged
@@ -172,6 +172,9 @@ class PeerLists:
         else:  # this rank's output rows as tensors (copied out after every merge)
             self.out_ids = _raw_view(self.out_ids_ptr(self.rank), (rows, k), torch.int32, device)
             self.out_vals = _raw_view(self.out_vals_ptr(self.rank), (rows, k), torch.float32, device)
+            # the other ranks' lists of this rank's row block, pulled in by the copy engines before the
+            # merge: [ids, value bits] x rank x (rows / world) x k
+            self.stage = torch.empty(2, self.world, rows // self.world, k, dtype=torch.int32, device=device)
         self.flag = torch.zeros(1, dtype=torch.int32, device=device)
         atexit.register(self.close)
 
@@ -189,7 +192,7 @@ class PeerLists:
 
     def close(self):
         lib = _lib.load()
-        self.out_ids = self.out_vals = None
+        self.out_ids = self.out_vals = self.stage = None
         for p in self.opened:
             lib.dsv32_ipc_close(ctypes.c_void_p(p))
         self.opened = []
@@ -256,8 +259,24 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     _mark(events, "order_allreduce")
     r = rows // world
     r0 = ex.rank * r
-    K.topk_parts_to_raw([ex.vals_ptr(j, r0) for j in range(world)], [ex.ids_ptr(j, r0) for j in range(world)],
-                        r, topk, topk, topk, [ex.out_ids_ptr(j, r0) for j in range(world)],
+    # The other ranks' lists of this row block into this GPU's memory by the copy engines (one
+    # cudaMemcpyAsync per rank and array, over NVLink), then the merge reads only local memory.
+    lib = _lib.load()
+    st = torch.cuda.current_stream(q.device).cuda_stream
+    nb = r * topk * 4
+    vals_p, ids_p = [], []
+    for j in range(world):
+        if j == ex.rank:
+            vals_p.append(ex.vals_ptr(j, r0))
+            ids_p.append(ex.ids_ptr(j, r0))
+            continue
+        di, dv = ex.stage[0, j].data_ptr(), ex.stage[1, j].data_ptr()
+        _lib.check(lib.dsv32_copy_async(di, ex.ids_ptr(j, r0), nb, st), "peer list copy")
+        _lib.check(lib.dsv32_copy_async(dv, ex.vals_ptr(j, r0), nb, st), "peer list copy")
+        vals_p.append(dv)
+        ids_p.append(di)
+    _mark(events, "pull_peer_lists")
+    K.topk_parts_to_raw(vals_p, ids_p, r, topk, topk, topk, [ex.out_ids_ptr(j, r0) for j in range(world)],
                         [ex.out_vals_ptr(j, r0) for j in range(world)], q.device, workspace=ex.ws_arg)
     _mark(events, "merge_to_every_rank")
     # A rank passes this all-reduce only after every rank's merge kernel has run, so its output rows

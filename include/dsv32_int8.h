@@ -211,6 +211,11 @@ int dsv32_topk_parts_to(const float* const* part_vals, const int32_t* const* par
 int dsv32_device_alloc(int64_t bytes, void** ptr);
 int dsv32_device_free(void* ptr);
 
+/* One asynchronous copy of `bytes` bytes on `stream` (cudaMemcpyAsync, any direction; between GPUs
+ * the copy engines move it over NVLink): the merge of key-sharded lists pulls the other ranks' rows
+ * into this GPU's memory with it (no reference counterpart). */
+int dsv32_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* CUDA IPC of such an allocation: export writes its DSV32_IPC_HANDLE_BYTES-byte handle; open maps a
  * handle exported by another process (peer access enabled on first use), close unmaps it. */
 #define DSV32_IPC_HANDLE_BYTES 64

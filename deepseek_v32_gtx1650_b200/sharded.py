@@ -9,10 +9,11 @@ Only the two paths that shard naturally are partitioned:
   It scores every query against its keys with the causal limit shifted by -lo and selects its
   local top-k (global key ids = lo + position). The lists are then merged by query row: each
   rank's selection lands in a buffer every rank maps with CUDA IPC (PeerLists), a one-element
-  all-reduce orders all selections before any read, rank r pulls the other ranks' lists of its rows /
-  world rows into its own memory with the copy engines and merges them with the top-k kernel, which
-  writes the merged rows into every rank's output buffer (dsv32_topk_parts_to), and a second
-  one-element all-reduce orders every merge before any rank reads its output. When the rows do not split
+  all-reduce orders all selections before any read, rank r merges its rows / world rows with the
+  top-k kernel (reading the other ranks' lists in place over NVLink, or with two ranks after pulling
+  the peer's into its own memory with the copy engines), which writes the merged rows into every
+  rank's output buffer (dsv32_topk_parts_to), and a second one-element all-reduce orders every merge
+  before any rank reads its output. When the rows do not split
   evenly or peer mappings are unavailable, merge_candidates does the exchange with NCCL
   all-to-alls (or an all-gather). Local lists are position-ordered and concatenated in rank order,
   so ties resolve to the lowest global key id exactly as in the single-GPU selection; the merged
@@ -172,9 +173,10 @@ class PeerLists:
         else:  # this rank's output rows as tensors (copied out after every merge)
             self.out_ids = _raw_view(self.out_ids_ptr(self.rank), (rows, k), torch.int32, device)
             self.out_vals = _raw_view(self.out_vals_ptr(self.rank), (rows, k), torch.float32, device)
-            # the other ranks' lists of this rank's row block, pulled in by the copy engines before the
-            # merge: [ids, value bits] x rank x (rows / world) x k
-            self.stage = torch.empty(2, self.world, rows // self.world, k, dtype=torch.int32, device=device)
+            # (two ranks) the peer's lists of this rank's row block, pulled in by the copy engines before
+            # the merge: [ids, value bits] x rank x (rows / world) x k
+            self.stage = (torch.empty(2, self.world, rows // self.world, k, dtype=torch.int32, device=device)
+                          if self.world == 2 else None)
         self.flag = torch.zeros(1, dtype=torch.int32, device=device)
         atexit.register(self.close)
 
@@ -259,14 +261,18 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
     _mark(events, "order_allreduce")
     r = rows // world
     r0 = ex.rank * r
-    # The other ranks' lists of this row block into this GPU's memory by the copy engines (one
-    # cudaMemcpyAsync per rank and array, over NVLink), then the merge reads only local memory.
+    # With two ranks the peer's lists of this row block are pulled into this GPU's memory by the copy
+    # engines first (one cudaMemcpyAsync per array, over NVLink) and the merge reads only local memory:
+    # 2 GPUs 2.874 -> 2.801 ms. With more ranks the copies, which run one after another on the stream,
+    # cost more than the merge kernel's own loads from the peers (4 GPUs 1.649 -> 1.726 ms, 8 GPUs
+    # 1.127 -> 1.281 ms), so the merge reads the peer lists in place.
+    pull = world == 2
     lib = _lib.load()
     st = torch.cuda.current_stream(q.device).cuda_stream
     nb = r * topk * 4
     vals_p, ids_p = [], []
     for j in range(world):
-        if j == ex.rank:
+        if j == ex.rank or not pull:
             vals_p.append(ex.vals_ptr(j, r0))
             ids_p.append(ex.ids_ptr(j, r0))
             continue
@@ -275,7 +281,8 @@ def sharded_index_topk(q, w, k_local, k_s_local, key_lo: int, topk: int = 2048, 
         _lib.check(lib.dsv32_copy_async(dv, ex.vals_ptr(j, r0), nb, st), "peer list copy")
         vals_p.append(dv)
         ids_p.append(di)
-    _mark(events, "pull_peer_lists")
+    if pull:
+        _mark(events, "pull_peer_lists")
     K.topk_parts_to_raw(vals_p, ids_p, r, topk, topk, topk, [ex.out_ids_ptr(j, r0) for j in range(world)],
                         [ex.out_vals_ptr(j, r0) for j in range(world)], q.device, workspace=ex.ws_arg)
     _mark(events, "merge_to_every_rank")

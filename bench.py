@@ -13,7 +13,7 @@ sharded by range over the ranks, strong scaling) with its per-stage times and a 
 merged selection against a one-GPU selection over all keys.
 Other workloads (--workload): gemm_down (K=2048 N=7168, --m), act_quant (--aq-dtype), index_prefill,
 index_decode (4 x 32768), index_long, index_step (rotate + quantise q/k, scores, top-2048),
-rotate_quant, weight_quant.
+rotate_quant, weight_quant, topk_merge (the per-rank merge of an 8-GPU key split on one GPU).
 
 Timing: W untimed warm-up steps, then K steps captured in one CUDA graph (multi-GPU steps with their
 NCCL calls) and replayed between CUDA events on the launching stream, a barrier + synchronize on
@@ -373,6 +373,84 @@ class ActQuantWorkload(Workload):
         dt, n = timed_loop(lambda: RT.act_quant_torch(x), seconds)
         return self.bytes / dt / 1e9, (f"torch on CPU: act_quant_torch (reference.py:38-40) on the whole "
                                        f"[{self.M}, {self.N}] {self.dt} input, {n} reps"), {}
+
+
+class TopkMergeWorkload(Workload):
+    """The merge step of the key-sharded indexer on one GPU: rows / world query rows, each the
+    concatenation of `parts` lists of k (value, global id) candidates read in place, top-k of each row
+    (select_topk_parts -> dsv32_topk_parts; the same kernel the sharded merge runs on the lists of
+    the other ranks, there read over NVLink). Default shape: the per-rank merge of an 8-GPU split of
+    the long context, 512 rows x 8 lists of 2048, top-2048 (two passes: 8192-candidate segments, then
+    the segment lists)."""
+    scaling = "weak"
+    dtype = "fp32"
+    higher_is_better = False
+
+    def __init__(self, rank, world, rows=512, parts=8, k=2048):
+        self.rows, self.parts, self.k = rows, parts, k
+        self.name = "topk_merge"
+        self.metric = f"top-k merge ms ({rows} rows x {parts} lists of {k}, top-{k})"
+        self.unit = "ms"
+        self.launches_per_step = 2
+        self.bytes = rows * parts * k * 8 + rows * k * 8  # candidate values + ids in, selection out
+        self.set_rotation(self.bytes, "list sets")
+
+    def config(self):
+        return {"workload": f"top-k merge of key-sharded lists: {self.rows} rows x {self.parts} lists of {self.k} "
+                            f"(the per-rank merge of an {self.parts}-GPU key split), top-{self.k}, lists read in place"}
+
+    def host_inputs(self):
+        g = torch.Generator().manual_seed(11)
+        vals = [torch.randn(self.rows, self.k, generator=g) for _ in range(self.parts)]
+        # each list position-ordered within its shard: increasing global ids
+        ids = [(torch.rand(self.rows, self.k, generator=g) * 16384).int().sort(dim=-1).values + j * 16384
+               for j in range(self.parts)]
+        return vals, ids
+
+    def prepare(self, dev):
+        import deepseek_v32_gtx1650_b200 as D
+        self.D = D
+        self.host = self.host_inputs()
+        self.sets = [([v.to(dev) for v in self.host[0]], [i.to(dev) for i in self.host[1]]) for _ in range(self.R)]
+
+    def step(self, i, ev=None, main_only=False):
+        vals, ids = self.sets[i % self.R]
+        self.D.select_topk_parts(vals, ids, self.k)
+
+    def value(self, ms, world):
+        return ms
+
+    def e2e_prepare(self, dev):
+        self.e2e_buffers(dev, tuple(t.pin_memory() for t in self.host[0] + self.host[1]),
+                         (torch.empty(self.rows, self.k, dtype=torch.int32).pin_memory(),
+                          torch.empty(self.rows, self.k).pin_memory()))
+
+    def e2e_run(self, din):
+        return self.D.select_topk_parts(list(din[:self.parts]), list(din[self.parts:]), self.k)
+
+    def roofline(self, kernel_ms, peaks, src, traffic):
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        ach = self.bytes / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": traffic.get(self.name), "peak_note": f"{src} STREAM-style copy; both passes of the step",
+                "algorithmic_bytes": self.bytes}
+
+    def cpu_sample(self, seconds):
+        """torch.topk on the host over each row's concatenated candidates (what the reference, which has
+        no merge step, would run on gathered lists), on a row sample."""
+        vals, ids = self.host if hasattr(self, "host") else self.host_inputs()
+        rows = min(self.rows, 64)
+        cv = torch.cat([v[:rows] for v in vals], -1)
+        ci = torch.cat([i[:rows] for i in ids], -1)
+
+        def run():
+            top = torch.topk(cv, self.k, dim=-1)
+            ci.gather(-1, top.indices)
+
+        dt, n = timed_loop(run, seconds)
+        return dt * 1e3 * (self.rows / rows), (f"torch on CPU: torch.topk over the concatenated {self.parts} x "
+                                                f"{self.k} candidates of {rows} of {self.rows} rows, {n} reps, "
+                                                f"scaled by rows"), {}
 
 
 def topk_launches(rows, n, k, reg_max=8192, temp_bytes=256 << 20, num_sms=148):
@@ -762,6 +840,8 @@ def make_workload(name, args, rank, world):
         return ProducerWorkload(name, rank, world)
     if name == "index_step":
         return IndexStepWorkload(rank, world)
+    if name == "topk_merge":
+        return TopkMergeWorkload(rank, world)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -992,7 +1072,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gemm_up",
                     choices=["gemm_up", "gemm_down", "act_quant", "index_prefill", "index_decode", "index_long",
-                             "rotate_quant", "weight_quant", "index_step"])
+                             "rotate_quant", "weight_quant", "index_step", "topk_merge"])
     ap.add_argument("--m", type=int, default=32, help="M for gemm_down")
     ap.add_argument("--long-queries", type=int, default=4096,
                     help="query rows of index_long (4096 = BASELINE's config; fewer for profiler captures)")
